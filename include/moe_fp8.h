@@ -1,0 +1,104 @@
+/*
+ * C-ABI of the B200 (sm_100a) DeepSeek-V3 FP8 block-scale fused-MoE operator.
+ *
+ * Drop-in for the operator `moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048`
+ * of LudensCS/starter-kit-fused-moe. All tensor pointers are device pointers;
+ * nothing here takes a framework type. Calls are asynchronous on the given
+ * CUDA stream and never synchronise the host (except moe_fp8_read_device_error).
+ */
+#ifndef MOE_FP8_H_
+#define MOE_FP8_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+#define MOE_OK 0
+#define MOE_ERR_INVALID_ARGUMENT 1   /* bad shape, null pointer, misaligned pointer */
+#define MOE_ERR_WORKSPACE 2          /* workspace missing or too small */
+#define MOE_ERR_CUDA 3               /* a CUDA runtime / driver call failed */
+#define MOE_ERR_DEVICE_TIMEOUT 4     /* a kernel gave up on a bounded wait (see moe_fp8_read_device_error) */
+
+/*
+ * Arguments of one operator call, in the reference's order.
+ * Replaces the 11-argument DPS entry point
+ *   run(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+ *       gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+ *       local_expert_offset, routed_scaling_factor, output)
+ * of solution/cuda/main.cpp:38-49 (TVM-FFI export at main.cpp:117) and
+ * solution/triton/current_kernel.py:1913-1925; shapes and dtypes as in
+ * resources/moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048.json:57-145.
+ */
+typedef struct MoeFp8Args {
+  const float* routing_logits;        /* f32  [T, 256] */
+  const void* routing_bias;           /* bf16 [256], or NULL for all-zero bias */
+  const void* hidden_states;          /* e4m3 [T, 7168] */
+  const float* hidden_states_scale;   /* f32  [56, T] (token-contiguous) */
+  const void* gemm1_weights;          /* e4m3 [E, 4096, 7168] */
+  const float* gemm1_weights_scale;   /* f32  [E, 32, 56] */
+  const void* gemm2_weights;          /* e4m3 [E, 7168, 2048] */
+  const float* gemm2_weights_scale;   /* f32  [E, 56, 16] */
+  int32_t local_expert_offset;        /* first global expert held here */
+  float routed_scaling_factor;        /* 2.5 for DeepSeek-V3 */
+  void* output;                       /* bf16 [T, 7168], fully overwritten */
+  int32_t num_tokens;                 /* T >= 0 */
+  int32_t num_local_experts;          /* E: 32 in the reference; 1..256 accepted */
+  void* workspace;                    /* device scratch, >= moe_fp8_workspace_bytes(T, E) */
+  size_t workspace_bytes;
+} MoeFp8Args;
+
+/*
+ * Runs routing -> permute -> GEMM1+SwiGLU -> GEMM2+combine on `stream`
+ * (a cudaStream_t; NULL = legacy default stream).
+ * Replaces solution/cuda/kernel.cu:60-109 (launch_moe_cuda) behind main.cpp:38.
+ */
+int moe_fp8_block_scale_run(const MoeFp8Args* args, void* stream);
+
+/* Workspace bytes for up to `max_tokens` tokens and `num_local_experts` experts.
+ * The reference keeps an equivalent op-owned cache (solution/cuda/kernel.cu:25-56,
+ * solution/triton/current_kernel.py:186-208); here the caller owns it. */
+size_t moe_fp8_workspace_bytes(int32_t max_tokens, int32_t num_local_experts);
+
+/* Routing only (kernel 1): writes topk ids / weights / per-expert counts into
+ * the workspace, readable through moe_fp8_workspace_view. Follows the routing
+ * step of the definition's reference (...json:146) and replaces
+ * solution/triton/current_kernel.py:211-314 (_routing_topk_kernel). */
+int moe_fp8_route(const float* routing_logits, const void* routing_bias, int32_t num_tokens,
+                  int32_t local_expert_offset, int32_t num_local_experts, float routed_scaling_factor,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device pointers into a workspace holding the state of the last call made
+ * with the same (num_tokens, num_local_experts). Exposes what the reference
+ * keeps in its internal buffers (topk ids / weights and per-expert counts of
+ * solution/triton/current_kernel.py:1307-1502). */
+typedef struct MoeFp8WorkspaceView {
+  int32_t* topk_idx;       /* [T, 8] selected global experts, descending biased score */
+  float* topk_weights;     /* [T, 8] combine weights */
+  int32_t* expert_counts;  /* [E] local pairs per expert */
+  int32_t* device_error;   /* sticky error bits of the kernels' bounded waits */
+  int32_t pair_capacity;   /* padded pair-row capacity */
+} MoeFp8WorkspaceView;
+int moe_fp8_workspace_view(void* workspace, int32_t num_tokens, int32_t num_local_experts,
+                           MoeFp8WorkspaceView* view);
+
+/* Reads (and clears) the device error word of a workspace; synchronises `stream`.
+ * Returns MOE_OK, or MOE_ERR_DEVICE_TIMEOUT with *bits set. The reference
+ * checks CUDA errors after its launches (solution/cuda/kernel.cu:19-23). */
+int moe_fp8_read_device_error(void* workspace, void* stream, int32_t* bits);
+
+/* Text of the last error on the calling thread (the reference raises the
+ * equivalent message through TVM_FFI_ICHECK, solution/cuda/main.cpp:20-34). */
+const char* moe_fp8_last_error(void);
+
+/* Number of kernels moe_fp8_block_scale_run launches for a given token count
+ * (the reference's launch sequence is solution/cuda/pure_moe.cu:564-662). */
+int32_t moe_fp8_kernels_per_call(int32_t num_tokens);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_FP8_H_ */

@@ -1,0 +1,434 @@
+// Kernels (3) and (4): FP8 block-scale grouped GEMMs on tcgen05.
+//
+// Both follow the reference's expert loop
+// (resources/moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048.json:146,
+// "3) Local expert compute and accumulation"):
+//   GEMM1  G1 = A_e W13_e^T (K = 7168), C = silu(G1[:, I:]) * G1[:, :I]
+//   GEMM2  O  = C W2_e^T    (K = 2048), output[token] += w * O
+// with A, W13, W2 dequantised by their 1x128 / 128x128 fp32 block scales.
+//
+// One persistent CTA per SM walks a device-built tile list
+// (expert, n-tile, m-tile), so no host synchronisation is needed for the
+// expert histogram. Inside a CTA, warps specialise:
+//   warp 0      TMA producer: A tile 128x128 and B tile 256x128 (FP8, 128-byte
+//               swizzle) per K-block into a 4-stage shared-memory ring;
+//   warp 1      allocates 512 TMEM columns and issues tcgen05.mma kind::f8f6f4
+//               (M=128, N=256, 4 x K=32 per K-block) into one of two TMEM
+//               partial accumulators;
+//   warps 2-9   promote every K-block's partial into registers with its block
+//               scales (acc += partial * sa[row, kb] * sb[n-block, kb]): the
+//               scales differ per K-block, so they are applied here, exactly
+//               once per 128-wide K-block, while the tensor core already runs
+//               the next K-block into the other TMEM buffer.
+// Epilogues:
+//   GEMM1  SwiGLU, then the 128 outputs of a row are re-quantised to FP8 as
+//          two terms (hi = e4m3(c/s), lo = e4m3((c - hi*s)/(s/16)), s = amax/448)
+//          stored as two consecutive rows of the GEMM2 operand, each with its
+//          own 1x128 scale; GEMM2 sums the pair, so the intermediate keeps
+//          about 8 bits of precision while GEMM2 stays on FP8 MMA.
+//   GEMM2  sums the hi/lo rows (lane pair shuffle), multiplies by the routing
+//          weight and adds into the fp32 token accumulator (vector atomics):
+//          the top-k combine happens here, with no separate reduce pass.
+#include "moe_common.cuh"
+#include "moe_kernels.h"
+
+namespace moe {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int A_TILE = BM * BK;  // 16 KB
+constexpr int B_TILE = BN * BK;  // 32 KB
+constexpr int STAGE_BYTES = A_TILE + B_TILE;
+constexpr int GEMM_THREADS = 320;
+constexpr int EPI_WARPS = 8;
+constexpr int TMEM_COLS = 512;
+
+struct GemmSmem {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t amax_bar[2];
+  uint32_t tmem_base;
+  int abort_flag;
+  int total_tiles;
+  int warp_sums[8];
+  int tile_start[kMaxLocalExperts + 1];
+  int mt_cnt[kMaxLocalExperts];
+  int row_off[kMaxLocalExperts];
+  int cnt[kMaxLocalExperts];
+  float amax_x[2][2][BM];
+};
+constexpr size_t GEMM_SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(GemmSmem);
+
+template <int MODE>
+struct GemmCfg;
+template <>
+struct GemmCfg<1> {
+  static constexpr int KB = kHiddenBlocks;   // 56 K-blocks over H
+  static constexpr int NT = kInter / 128;    // 16 n-tiles: 128 gate + 128 up columns each
+  static constexpr int ROWS_PER_PAIR = 1;
+};
+template <>
+struct GemmCfg<2> {
+  static constexpr int KB = kInterBlocks;    // 16 K-blocks over I
+  static constexpr int NT = kHidden / BN;    // 28 n-tiles of 256 output columns
+  static constexpr int ROWS_PER_PAIR = 2;    // hi and lo term rows
+};
+
+// Block-wide exclusive scan of one int per thread over threads < 256.
+__device__ __forceinline__ int block_scan_256(int v, int* warp_sums, int& total) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  int inc = v;
+  if (tid < 256) {
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, inc, d);
+      if (lane >= d) inc += n;
+    }
+    if (lane == 31) warp_sums[w] = inc;
+  }
+  __syncthreads();
+  int pre = 0, tot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int s = warp_sums[i];
+    if (i < w) pre += s;
+    tot += s;
+  }
+  total = tot;
+  __syncthreads();
+  return pre + inc - v;
+}
+
+__device__ __forceinline__ void decode_tile(const GemmSmem& S, int E, int t, int& e, int& nt, int& mt) {
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (S.tile_start[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  e = lo;
+  const int local = t - S.tile_start[e];
+  const int m = S.mt_cnt[e];
+  nt = local / m;
+  mt = local - nt * m;
+}
+
+__device__ __forceinline__ void set_abort(GemmSmem& S, int* err, int code) {
+  atomicOr(err, code);
+  *reinterpret_cast<volatile int*>(&S.abort_flag) = 1;
+}
+__device__ __forceinline__ bool aborted(const GemmSmem& S) {
+  return *reinterpret_cast<const volatile int*>(&S.abort_flag) != 0;
+}
+
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return (uint32_t)lo | ((uint32_t)hi << 16);
+}
+__device__ __forceinline__ float2 unpack_e4m3x2(uint32_t v16) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v16, __NV_E4M3);
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmArgs args) {
+  using Cfg = GemmCfg<MODE>;
+  constexpr int KB = Cfg::KB, NT = Cfg::NT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  GemmSmem& S = *reinterpret_cast<GemmSmem*>(smem + STAGES * STAGE_BYTES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = args.E;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&S.full[s]), 1);
+      mbar_init(smem_u32(&S.empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&S.tfull[b]), 1);
+      mbar_init(smem_u32(&S.tempty[b]), EPI_WARPS);
+      mbar_init(smem_u32(&S.amax_bar[b]), EPI_WARPS);
+    }
+    S.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  // tile list from the device-side expert histogram
+  {
+    const int tid = threadIdx.x;
+    const int c = (tid < E) ? args.counts[tid] : 0;
+    const int mt = (c * Cfg::ROWS_PER_PAIR + BM - 1) / BM;
+    int tot0, tot1;
+    const int roff = block_scan_256(align_up(c, 128), S.warp_sums, tot0);
+    const int tstart = block_scan_256(mt * NT, S.warp_sums, tot1);
+    if (tid < E) {
+      S.cnt[tid] = c;
+      S.mt_cnt[tid] = mt;
+      S.row_off[tid] = roff;
+      S.tile_start[tid] = tstart;
+    }
+    if (tid == 0) {
+      S.tile_start[E] = tot1;
+      S.total_tiles = tot1;
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&S.tmem_base), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = S.tmem_base;
+  const int total = S.total_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
+        int e, nt, mt;
+        decode_tile(S, E, t, e, nt, mt);
+        const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES, u = it / STAGES;
+          if (!mbar_wait(smem_u32(&S.empty[s]), (u & 1) ^ 1)) {
+            set_abort(S, args.err, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&S.full[s]);
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_TILE;
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          tma_load_2d(sa, &tmA, fb, kb * BK, arow);
+          if (MODE == 1) {
+            tma_load_2d(sb, &tmB, fb, kb * BK, e * kGemm1N + nt * 128);
+            tma_load_2d(sb + B_TILE / 2, &tmB, fb, kb * BK, e * kGemm1N + kInter + nt * 128);
+          } else {
+            tma_load_2d(sb, &tmB, fb, kb * BK, e * kHidden + nt * BN);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
+      int it = 0, kt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
+        for (int kb = 0; kb < KB; ++kb, ++it, ++kt) {
+          const int s = it % STAGES, u = it / STAGES;
+          const int b = kt & 1, v = kt >> 1;
+          if (!mbar_wait(smem_u32(&S.tempty[b]), (v & 1) ^ 1) || !mbar_wait(smem_u32(&S.full[s]), u & 1)) {
+            set_abort(S, args.err, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + (uint32_t)(b * BN);
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_TILE;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            mma_e4m3(d, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc, kk > 0 ? 1u : 0u);
+          mma_commit(smem_u32(&S.empty[s]));
+          mma_commit(smem_u32(&S.tfull[b]));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ promotion + epilogue
+    const int ew = warp - 2;
+    const int q = warp & 3;          // TMEM lane quadrant this warp may access
+    const int g = ew >> 2;           // column half
+    const int r = 32 * q + lane;     // row inside the tile
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(32 * q) << 16);
+    int kt = 0, tile_iter = 0;
+    for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++tile_iter) {
+      int e, nt, mt;
+      decode_tile(S, E, t, e, nt, mt);
+      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
+      const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + row_in_expert;
+      const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
+      const size_t ld_sa = (size_t)Cfg::ROWS_PER_PAIR * args.R1;
+      // weight block scales for this tile
+      const float* sbp;
+      const float* sbp2 = nullptr;
+      if (MODE == 1) {
+        sbp = args.sb + ((size_t)e * 32 + nt) * kHiddenBlocks;           // gate block row
+        sbp2 = args.sb + ((size_t)e * 32 + 16 + nt) * kHiddenBlocks;     // up block row
+      } else {
+        sbp = args.sb + ((size_t)e * kHiddenBlocks + 2 * nt + g) * kInterBlocks;
+      }
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      float sa_next = __ldg(args.sa + arow);
+      float sb_next = __ldg(sbp);
+      float sb2_next = MODE == 1 ? __ldg(sbp2) : 0.f;
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb, ++kt) {
+        const float sa_cur = sa_next, sb_cur = sb_next, sb2_cur = sb2_next;
+        if (kb + 1 < KB) {
+          sa_next = __ldg(args.sa + (size_t)(kb + 1) * ld_sa + arow);
+          sb_next = __ldg(sbp + kb + 1);
+          if (MODE == 1) sb2_next = __ldg(sbp2 + kb + 1);
+        }
+        const int b = kt & 1, v = kt >> 1;
+        if (!mbar_wait(smem_u32(&S.tfull[b]), v & 1)) {
+          set_abort(S, args.err, kErrTimeoutEpilogue);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = lane_addr + (uint32_t)(b * BN);
+        const float f0 = sa_cur * sb_cur;
+        const float f1 = MODE == 1 ? sa_cur * sb2_cur : f0;
+#pragma unroll
+        for (int c = 0; c < 8; c += 2) {
+          // MODE 1: chunks 0-3 = gate columns 64g.., chunks 4-7 = up columns 128+64g..
+          const int col0 = MODE == 1 ? (c < 4 ? 64 * g + 16 * c : 128 + 64 * g + 16 * (c - 4)) : 128 * g + 16 * c;
+          float p0[16], p1[16];
+          tmem_ld16(base + col0, p0);
+          tmem_ld16(base + col0 + 16, p1);
+          tmem_ld_wait();
+          const float f = c < 4 ? f0 : f1;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            acc[16 * c + i] = fmaf(p0[i], f, acc[16 * c + i]);
+            acc[16 * c + 16 + i] = fmaf(p1[i], f, acc[16 * c + 16 + i]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&S.tempty[b]));
+      }
+      if (!ok) break;
+
+      if (MODE == 1) {
+        // SwiGLU: C = silu(X2) * X1 with X1 = gate half (cols < I), X2 = up half
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const float x1 = acc[j], x2 = acc[64 + j];
+          const float c = (x2 / (1.0f + expf(-x2))) * x1;
+          acc[j] = c;
+          amax = fmaxf(amax, fabsf(c));
+        }
+        // exchange the row maximum with the warp that holds the other 64 columns
+        const int xb = tile_iter & 1;
+        S.amax_x[xb][g][r] = amax;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&S.amax_bar[xb]));
+        if (!mbar_wait(smem_u32(&S.amax_bar[xb]), (tile_iter >> 1) & 1)) {
+          set_abort(S, args.err, kErrTimeoutEpilogue);
+          break;
+        }
+        amax = fmaxf(amax, S.amax_x[xb][g ^ 1][r]);
+        if (valid) {
+          const float s_hi = amax / kFp8Max;
+          const float inv_hi = amax > 0.f ? kFp8Max / amax : 0.f;
+          const float s_lo = s_hi * (1.0f / 16.0f);
+          const float inv_lo = inv_hi * 16.0f;
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int j4 = 0; j4 < 16; ++j4) {
+            float c[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c[i] = acc[4 * j4 + i];
+            hi[j4] = pack_e4m3x4(c[0] * inv_hi, c[1] * inv_hi, c[2] * inv_hi, c[3] * inv_hi);
+            const float2 h01 = unpack_e4m3x2(hi[j4] & 0xffffu);
+            const float2 h23 = unpack_e4m3x2(hi[j4] >> 16);
+            lo[j4] = pack_e4m3x4((c[0] - h01.x * s_hi) * inv_lo, (c[1] - h01.y * s_hi) * inv_lo,
+                                 (c[2] - h23.x * s_hi) * inv_lo, (c[3] - h23.y * s_hi) * inv_lo);
+          }
+          const size_t prow = (size_t)S.row_off[e] + row_in_expert;  // pair row
+          uint8_t* dhi = args.a2 + (2 * prow) * kInter + nt * 128 + 64 * g;
+          uint8_t* dlo = dhi + kInter;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            reinterpret_cast<uint4*>(dhi)[k] = make_uint4(hi[4 * k], hi[4 * k + 1], hi[4 * k + 2], hi[4 * k + 3]);
+            reinterpret_cast<uint4*>(dlo)[k] = make_uint4(lo[4 * k], lo[4 * k + 1], lo[4 * k + 2], lo[4 * k + 3]);
+          }
+          if (g == 0) {
+            float* sa2 = args.sa2 + (size_t)nt * 2 * args.R1 + 2 * prow;
+            sa2[0] = s_hi;
+            sa2[1] = s_lo;
+          }
+        }
+      } else {
+        // combine: (hi row + lo row) * routing weight -> fp32 token accumulator
+        const int odd = lane & 1;
+        const int pair = row_in_expert >> 1;
+        const size_t prow = (size_t)S.row_off[e] + pair;
+        int token = 0;
+        float w = 0.f;
+        if (valid) {
+          token = __ldg(args.row_token + prow);
+          w = __ldg(args.row_weight + prow);
+        }
+        float* dst = args.out_acc + (size_t)token * kHidden + nt * BN + 128 * g + (odd ? 64 : 0);
+#pragma unroll
+        for (int j4 = 0; j4 < 16; ++j4) {
+          float o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int j = 4 * j4 + i;
+            const float a = acc[j], bb = acc[64 + j];
+            const float send = odd ? a : bb;
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            const float mine = odd ? bb : a;
+            o[i] = (mine + recv) * w;
+          }
+          if (valid) atomicAdd(reinterpret_cast<float4*>(dst) + j4, make_float4(o[0], o[1], o[2], o[3]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+static int g_smem_set[2][64];
+
+template <int MODE>
+cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
+                          cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !g_smem_set[MODE - 1][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)GEMM_SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) g_smem_set[MODE - 1][dev] = 1;
+  }
+  grouped_gemm_kernel<MODE><<<num_sms, GEMM_THREADS, GEMM_SMEM_BYTES, st>>>(tmA, tmB, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
+                         cudaStream_t st) {
+  return launch_gemm_t<1>(tmA, tmB, args, num_sms, st);
+}
+cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
+                         cudaStream_t st) {
+  return launch_gemm_t<2>(tmA, tmB, args, num_sms, st);
+}
+
+}  // namespace moe

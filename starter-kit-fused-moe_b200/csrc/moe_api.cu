@@ -1,0 +1,228 @@
+// C-ABI layer: argument checks, workspace carving, TMA descriptors and the
+// launch sequence route -> permute -> GEMM1 -> GEMM2 -> finalize.
+//
+// Mirrors the reference's CUDA entry (solution/cuda/main.cpp:38-117: shape and
+// dtype checks, then launch on the caller's stream) and its launcher
+// (solution/cuda/kernel.cu:60-109), without any host synchronisation: the
+// per-expert histogram stays on the device and the GEMM kernels build their
+// tile lists from it.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "moe_fp8.h"
+#include "moe_common.cuh"
+#include "moe_kernels.h"
+#include "moe_workspace.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D byte tensor [rows, cols] (row-major), tile box [box_rows, 128 bytes], 128-byte swizzle.
+bool encode_fp8_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms_of_current_device() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_workspace(void* ws, size_t bytes, int T, int E) {
+  if (!ws) return fail(MOE_ERR_WORKSPACE, "workspace is NULL");
+  if (!aligned(ws, 256)) return fail(MOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  const size_t need = moe::ws_layout(T, E).total;
+  if (bytes < need)
+    return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes, got " +
+                                       std::to_string(bytes));
+  return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* moe_fp8_last_error(void) { return g_last_error.c_str(); }
+
+size_t moe_fp8_workspace_bytes(int32_t max_tokens, int32_t num_local_experts) {
+  if (max_tokens < 0 || num_local_experts < 1 || num_local_experts > moe::kMaxLocalExperts) return 0;
+  return moe::ws_layout(max_tokens, num_local_experts).total;
+}
+
+int32_t moe_fp8_kernels_per_call(int32_t num_tokens) { return num_tokens > 0 ? 5 : 0; }
+
+int moe_fp8_workspace_view(void* workspace, int32_t T, int32_t E, MoeFp8WorkspaceView* view) {
+  if (!workspace || !view || T < 0 || E < 1 || E > moe::kMaxLocalExperts)
+    return fail(MOE_ERR_INVALID_ARGUMENT, "bad workspace view request");
+  const moe::WsLayout L = moe::ws_layout(T, E);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  view->topk_idx = reinterpret_cast<int32_t*>(w + L.topk_idx);
+  view->topk_weights = reinterpret_cast<float*>(w + L.topk_w);
+  view->expert_counts = reinterpret_cast<int32_t*>(w + L.counts);
+  view->device_error = reinterpret_cast<int32_t*>(w + L.err);
+  view->pair_capacity = L.R1;
+  return MOE_OK;
+}
+
+int moe_fp8_read_device_error(void* workspace, void* stream, int32_t* bits) {
+  if (!workspace || !bits) return fail(MOE_ERR_INVALID_ARGUMENT, "NULL argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* dev = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + moe::ws_layout(0, 1).err);
+  int32_t h = 0;
+  cudaError_t e = cudaMemcpyAsync(&h, dev, sizeof(h), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dev, 0, sizeof(int32_t), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  *bits = h;
+  if (h) return fail(MOE_ERR_DEVICE_TIMEOUT, "a kernel gave up on a bounded wait (bits " + std::to_string(h) + ")");
+  return MOE_OK;
+}
+
+int moe_fp8_route(const float* logits, const void* bias, int32_t T, int32_t offset, int32_t E, float scale,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (T < 0 || E < 1 || E > moe::kMaxLocalExperts) return fail(MOE_ERR_INVALID_ARGUMENT, "bad T or E");
+  if (T > 0 && (!logits || !aligned(logits, 16)))
+    return fail(MOE_ERR_INVALID_ARGUMENT, "routing_logits must be a 16-byte aligned device pointer");
+  if (bias && !aligned(bias, 16)) return fail(MOE_ERR_INVALID_ARGUMENT, "routing_bias must be 16-byte aligned");
+  if (int rc = check_workspace(workspace, workspace_bytes, T, E)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const moe::WsLayout L = moe::ws_layout(T, E);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(w + L.counts, 0, sizeof(int32_t) * E, st);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
+  e = moe::launch_route(logits, static_cast<const __nv_bfloat16*>(bias), T, offset, E, scale,
+                        reinterpret_cast<int*>(w + L.topk_idx), reinterpret_cast<float*>(w + L.topk_w),
+                        reinterpret_cast<int*>(w + L.pair_pos), reinterpret_cast<int*>(w + L.counts), nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
+  return MOE_OK;
+}
+
+int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
+  if (!a) return fail(MOE_ERR_INVALID_ARGUMENT, "args is NULL");
+  const int T = a->num_tokens, E = a->num_local_experts;
+  if (T < 0) return fail(MOE_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
+  if (E < 1 || E > moe::kMaxLocalExperts)
+    return fail(MOE_ERR_INVALID_ARGUMENT, "num_local_experts must be in [1, 256]");
+  if (T == 0) return MOE_OK;
+  if (!a->routing_logits || !a->hidden_states || !a->hidden_states_scale || !a->gemm1_weights ||
+      !a->gemm1_weights_scale || !a->gemm2_weights || !a->gemm2_weights_scale || !a->output)
+    return fail(MOE_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (!aligned(a->routing_logits, 16) || !aligned(a->hidden_states, 16) || !aligned(a->gemm1_weights, 16) ||
+      !aligned(a->gemm2_weights, 16) || !aligned(a->output, 16) ||
+      (a->routing_bias && !aligned(a->routing_bias, 16)) || !aligned(a->hidden_states_scale, 4) ||
+      !aligned(a->gemm1_weights_scale, 4) || !aligned(a->gemm2_weights_scale, 4))
+    return fail(MOE_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned (scales 4-byte)");
+  if (int rc = check_workspace(a->workspace, a->workspace_bytes, T, E)) return rc;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nsm = num_sms_of_current_device();
+  const moe::WsLayout L = moe::ws_layout(T, E);
+  uint8_t* w = static_cast<uint8_t*>(a->workspace);
+  int* counts = reinterpret_cast<int*>(w + L.counts);
+  int* topk_idx = reinterpret_cast<int*>(w + L.topk_idx);
+  float* topk_w = reinterpret_cast<float*>(w + L.topk_w);
+  int* pair_pos = reinterpret_cast<int*>(w + L.pair_pos);
+  int* row_token = reinterpret_cast<int*>(w + L.row_token);
+  float* row_weight = reinterpret_cast<float*>(w + L.row_weight);
+  uint8_t* a1 = w + L.a1;
+  float* sa1 = reinterpret_cast<float*>(w + L.sa1);
+  uint8_t* a2 = w + L.a2;
+  float* sa2 = reinterpret_cast<float*>(w + L.sa2);
+  float* acc = reinterpret_cast<float*>(w + L.out_acc);
+  int* err = reinterpret_cast<int*>(w + L.err);
+
+  CUtensorMap tmA1, tmB1, tmA2, tmB2;
+  if (!encode_fp8_2d(&tmA1, a1, moe::kHidden, L.R1, 128) ||
+      !encode_fp8_2d(&tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128) ||
+      !encode_fp8_2d(&tmA2, a2, moe::kInter, 2ull * L.R1, 128) ||
+      !encode_fp8_2d(&tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, 256))
+    return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+
+  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
+  e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
+                        a->local_expert_offset, E, a->routed_scaling_factor, topk_idx, topk_w, pair_pos, counts, acc,
+                        st);
+  if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
+  e = moe::launch_permute(static_cast<const uint8_t*>(a->hidden_states), a->hidden_states_scale, T, E,
+                          a->local_expert_offset, topk_idx, topk_w, pair_pos, counts, L.R1, a1, sa1, row_token,
+                          row_weight, nsm, st);
+  if (e != cudaSuccess) return cuda_fail(e, "permute kernel launch");
+
+  moe::GemmArgs g1{};
+  g1.counts = counts;
+  g1.E = E;
+  g1.R1 = L.R1;
+  g1.sa = sa1;
+  g1.sb = a->gemm1_weights_scale;
+  g1.a2 = a2;
+  g1.sa2 = sa2;
+  g1.err = err;
+  e = moe::launch_gemm1(tmA1, tmB1, g1, nsm, st);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMM1 launch");
+
+  moe::GemmArgs g2{};
+  g2.counts = counts;
+  g2.E = E;
+  g2.R1 = L.R1;
+  g2.sa = sa2;
+  g2.sb = a->gemm2_weights_scale;
+  g2.row_token = row_token;
+  g2.row_weight = row_weight;
+  g2.out_acc = acc;
+  g2.err = err;
+  e = moe::launch_gemm2(tmA2, tmB2, g2, nsm, st);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMM2 launch");
+
+  e = moe::launch_finalize(acc, static_cast<__nv_bfloat16*>(a->output), T, nsm, st);
+  if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
+  return MOE_OK;
+}
+
+}  // extern "C"

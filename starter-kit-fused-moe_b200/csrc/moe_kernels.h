@@ -1,0 +1,36 @@
+// Internal launch interface between the C-ABI layer and the kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+struct GemmArgs {
+  const int* counts;       // [E] pairs per local expert
+  int E;                   // local experts
+  int R1;                  // pair-row capacity of the workspace
+  const float* sa;         // GEMM1: [56, R1] activation scales; GEMM2: [16, 2*R1]
+  const float* sb;         // GEMM1: [E, 32, 56] W13 scales;     GEMM2: [E, 56, 16] W2 scales
+  uint8_t* a2;             // GEMM1 out: e4m3 [2*R1, 2048]
+  float* sa2;              // GEMM1 out: [16, 2*R1]
+  const int* row_token;    // GEMM2: token of each pair row
+  const float* row_weight; // GEMM2: routing weight of each pair row
+  float* out_acc;          // GEMM2 out: f32 [T, 7168]
+  int* err;                // device error word
+};
+
+cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
+                         int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
+                         cudaStream_t st);
+cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E, int offset, const int* topk_idx,
+                           const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
+                           float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st);
+cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, int num_sms, cudaStream_t st);
+cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
+                         cudaStream_t st);
+cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
+                         cudaStream_t st);
+
+}  // namespace moe

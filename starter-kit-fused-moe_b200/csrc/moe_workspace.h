@@ -1,0 +1,60 @@
+// Layout of the operator's device workspace (one contiguous byte buffer owned
+// by the caller and reused across calls).
+//
+// Pair rows: every (token, local expert) selection is one "pair row". Pair rows
+// are grouped expert-major and each expert's group is padded to 128 rows so a
+// 128-row GEMM tile never straddles two experts. For T tokens and E local
+// experts at most min(8, E) * T + 127 * E rows are used; `R1` rounds that up
+// to 128.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+namespace moe {
+
+struct WsLayout {
+  int T, E, R1;               // tokens, local experts, pair-row capacity
+  size_t err;                 // int32 error word (sticky; cleared by the host reader)
+  size_t counts;              // int32 [E]   pairs per local expert
+  size_t topk_idx;            // int32 [T*8] selected global experts (selection order)
+  size_t topk_w;              // f32   [T*8] combine weights
+  size_t pair_pos;            // int32 [T*8] position inside the expert's group, -1 if not local
+  size_t row_token;           // int32 [R1]  token of each pair row
+  size_t row_weight;          // f32   [R1]  combine weight of each pair row
+  size_t a1;                  // e4m3  [R1, 7168]   gathered activations
+  size_t sa1;                 // f32   [56, R1]     their 1x128 scales (row-contiguous)
+  size_t a2;                  // e4m3  [2*R1, 2048] SwiGLU output, two FP8 terms per pair row
+  size_t sa2;                 // f32   [16, 2*R1]   their 1x128 scales
+  size_t out_acc;             // f32   [T, 7168]    combine accumulator
+  size_t total;
+};
+
+inline size_t ws_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline WsLayout ws_layout(int T, int E) {
+  WsLayout L{};
+  L.T = T;
+  L.E = E;
+  const int k = E < 8 ? E : 8;
+  long long rows = (long long)k * T + 127LL * E;
+  L.R1 = (int)((rows + 127) / 128 * 128);
+  if (L.R1 < 128) L.R1 = 128;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t r = o; o = ws_align(o + bytes, 1024); return r; };
+  L.err = take(256);
+  L.counts = take(sizeof(int32_t) * 256);
+  L.topk_idx = take(sizeof(int32_t) * 8 * (size_t)T);
+  L.topk_w = take(sizeof(float) * 8 * (size_t)T);
+  L.pair_pos = take(sizeof(int32_t) * 8 * (size_t)T);
+  L.row_token = take(sizeof(int32_t) * (size_t)L.R1);
+  L.row_weight = take(sizeof(float) * (size_t)L.R1);
+  L.a1 = take((size_t)L.R1 * 7168);
+  L.sa1 = take(sizeof(float) * 56 * (size_t)L.R1);
+  L.a2 = take((size_t)2 * L.R1 * 2048);
+  L.sa2 = take(sizeof(float) * 16 * 2 * (size_t)L.R1);
+  L.out_acc = take(sizeof(float) * 7168 * (size_t)T);
+  L.total = o;
+  return L;
+}
+
+}  // namespace moe

@@ -1,0 +1,261 @@
+// Kernel (1) DeepSeek-V3 no-aux routing, kernel (2) permute/gather, and the
+// final fp32 -> bf16 pass.
+//
+// Routing restates the reference's routing step
+// (resources/moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048.json:146,
+// "2) No-aux routing"): s = sigmoid(logit), sb = s + bias, group score = sum of
+// the two largest sb of each 32-expert group, keep the 4 best groups, pick the
+// 8 largest sb among their experts, weight = s / (sum of the 8 s + 1e-20) * scale.
+// Unlike solution/triton/current_kernel.py:246-247 no index-dependent tie-break
+// is added to the scores: exact ties go to the lower index, everything else is
+// decided on the raw fp32 values, so the selected sets equal the reference's.
+#include "moe_common.cuh"
+#include "moe_kernels.h"
+
+namespace moe {
+
+constexpr int kRouteWarps = 8;
+constexpr int kRouteTokensPerWarp = 4;
+constexpr int kRouteTokensPerBlock = kRouteWarps * kRouteTokensPerWarp;
+
+__device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// One warp per token; lane l owns experts 8l..8l+7, so lanes 4g..4g+3 hold group g.
+// Local selections are counted per block in shared memory and published with
+// one global atomic per (block, expert); each selection gets its position
+// inside its expert's group (pair_pos), -1 when the expert is not local.
+__global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
+    const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, int T, int offset, int E,
+    float scale, int* __restrict__ topk_idx, float* __restrict__ topk_w, int* __restrict__ pair_pos,
+    int* __restrict__ counts, float* __restrict__ out_acc) {
+  __shared__ int hist[kMaxLocalExperts];
+  __shared__ int base[kMaxLocalExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+
+  int my_le[kRouteTokensPerWarp], my_lpos[kRouteTokensPerWarp];
+#pragma unroll
+  for (int i = 0; i < kRouteTokensPerWarp; ++i) {
+    my_le[i] = -1;
+    my_lpos[i] = 0;
+    const int t = blockIdx.x * kRouteTokensPerBlock + warp * kRouteTokensPerWarp + i;
+    if (t >= T) continue;  // warp-uniform
+    const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExperts + lane * 8);
+    const float4 x0 = __ldg(lp), x1 = __ldg(lp + 1);
+    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    float b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (bias != nullptr) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(bias + lane * 8));
+      const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(bp[j]);
+        b[2 * j] = f.x;
+        b[2 * j + 1] = f.y;
+      }
+    }
+    float sb[8];
+    float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sb[j] = sigmoid_ref(x[j]) + b[j];
+      if (sb[j] > m1) {
+        m2 = m1;
+        m1 = sb[j];
+      } else if (sb[j] > m2) {
+        m2 = sb[j];
+      }
+    }
+    // merge the top-2 of the group's four lanes
+#pragma unroll
+    for (int d = 1; d <= 2; d <<= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, m1, d);
+      const float o2 = __shfl_xor_sync(0xffffffffu, m2, d);
+      const float n1 = fmaxf(m1, o1);
+      const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+      m1 = n1;
+      m2 = n2;
+    }
+    const float gscore = m1 + m2;
+    const int mygroup = lane >> 2;
+    int rank = 0;
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) {
+      const float gs = __shfl_sync(0xffffffffu, gscore, 4 * g);
+      rank += (gs > gscore) || (gs == gscore && g < mygroup);
+    }
+    const bool keep = rank < kTopKGroups;
+
+    // 8 rounds of warp argmax over the kept experts (ties -> lower index)
+    uint32_t removed = keep ? 0u : 0xffu;
+    int sel = 0;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (!((removed >> j) & 1u) && (bi == 0x7fffffff || sb[j] > bv)) {
+          bv = sb[j];
+          bi = lane * 8 + j;
+        }
+      }
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+        if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if ((bi >> 3) == lane) removed |= 1u << (bi & 7);
+      if (lane == k) sel = bi;
+    }
+    // combine weights from the un-biased sigmoid (recomputed: same input, same value)
+    const float s_sel = lane < kTopK ? sigmoid_ref(__ldg(logits + (size_t)t * kExperts + sel)) : 0.f;
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) sum += __shfl_sync(0xffffffffu, s_sel, k);
+    if (lane < kTopK) {
+      const float w = (s_sel / (sum + 1e-20f)) * scale;
+      topk_idx[(size_t)t * kTopK + lane] = sel;
+      topk_w[(size_t)t * kTopK + lane] = w;
+      const int le = sel - offset;
+      if (le >= 0 && le < E) {
+        my_le[i] = le;
+        my_lpos[i] = atomicAdd(&hist[le], 1);
+      }
+    }
+    // clear this token's combine accumulator row
+    if (out_acc != nullptr) {
+      float4* row = reinterpret_cast<float4*>(out_acc + (size_t)t * kHidden);
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = lane; c < kHidden / 4; c += 32) row[c] = z;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] = hist[e] ? atomicAdd(&counts[e], hist[e]) : 0;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kRouteTokensPerWarp; ++i) {
+    const int t = blockIdx.x * kRouteTokensPerBlock + warp * kRouteTokensPerWarp + i;
+    if (t < T && lane < kTopK) pair_pos[(size_t)t * kTopK + lane] = my_le[i] >= 0 ? base[my_le[i]] + my_lpos[i] : -1;
+  }
+}
+
+// Exclusive scan of align_up(counts[e], 128) over e < E (E <= 256) into off[];
+// called by every thread of a 256-thread block.
+__device__ void padded_offsets_256(const int* __restrict__ counts, int E, int* off, int* warp_sums) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int v = tid < E ? align_up(counts[tid], 128) : 0;
+  int inc = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += n;
+  }
+  if (lane == 31) warp_sums[w] = inc;
+  __syncthreads();
+  int pre = 0;
+  for (int i = 0; i < w; ++i) pre += warp_sums[i];
+  off[tid] = pre + inc - v;
+  __syncthreads();
+}
+
+// One warp per token: the token's FP8 row is read once (16-byte loads) and
+// written to each of its local pair rows; scales are transposed into the
+// row-contiguous [56, R1] layout the GEMM epilogue reads.
+__global__ void __launch_bounds__(256) permute_kernel(
+    const uint8_t* __restrict__ hidden, const float* __restrict__ hs, int T, int E, int offset,
+    const int* __restrict__ topk_idx, const float* __restrict__ topk_w, const int* __restrict__ pair_pos,
+    const int* __restrict__ counts, int R1, uint8_t* __restrict__ a1, float* __restrict__ sa1,
+    int* __restrict__ row_token, float* __restrict__ row_weight) {
+  __shared__ int off[256];
+  __shared__ int warp_sums[8];
+  padded_offsets_256(counts, E, off, warp_sums);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
+    int pp = -1, ge = 0;
+    float w = 0.f;
+    if (lane < kTopK) {
+      pp = pair_pos[(size_t)t * kTopK + lane];
+      ge = topk_idx[(size_t)t * kTopK + lane];
+      w = topk_w[(size_t)t * kTopK + lane];
+    }
+    const uint32_t any = __ballot_sync(0xffffffffu, pp >= 0);
+    if (!any) continue;
+    constexpr int kVec = kHidden / 16;  // 448 uint4 per row
+    constexpr int kPer = kVec / 32;     // 14 per lane
+    uint4 v[kPer];
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) v[i] = __ldg(src + lane + 32 * i);
+    const float s0 = lane < kHiddenBlocks ? __ldg(hs + (size_t)lane * T + t) : 0.f;
+    const float s1 = lane + 32 < kHiddenBlocks ? __ldg(hs + (size_t)(lane + 32) * T + t) : 0.f;
+    uint32_t m = any;
+    while (m) {
+      const int k = __ffs(m) - 1;
+      m &= m - 1;
+      const int kpp = __shfl_sync(0xffffffffu, pp, k);
+      const int kge = __shfl_sync(0xffffffffu, ge, k);
+      const float kw = __shfl_sync(0xffffffffu, w, k);
+      const int row = off[kge - offset] + kpp;
+      uint4* dst = reinterpret_cast<uint4*>(a1 + (size_t)row * kHidden);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) dst[lane + 32 * i] = v[i];
+      if (lane < kHiddenBlocks) sa1[(size_t)lane * R1 + row] = s0;
+      if (lane + 32 < kHiddenBlocks) sa1[(size_t)(lane + 32) * R1 + row] = s1;
+      if (lane == 0) {
+        row_token[row] = t;
+        row_weight[row] = kw;
+      }
+    }
+  }
+}
+
+// out[i] = bf16(acc[i]), 8 elements per thread-iteration.
+__global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out,
+                                                       size_t n8) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
+    __nv_bfloat162 r[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                           __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+    reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<uint4*>(r);
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
+                         int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
+                         cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const int grid = (T + kRouteTokensPerBlock - 1) / kRouteTokensPerBlock;
+  route_kernel<<<grid, kRouteWarps * 32, 0, st>>>(logits, bias, T, offset, E, scale, topk_idx, topk_w, pair_pos,
+                                                  counts, out_acc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E, int offset, const int* topk_idx,
+                           const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
+                           float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  int grid = (T + 7) / 8;
+  if (grid > num_sms * 8) grid = num_sms * 8;
+  permute_kernel<<<grid, 256, 0, st>>>(hidden, hs, T, E, offset, topk_idx, topk_w, pair_pos, counts, R1, a1, sa1,
+                                       row_token, row_weight);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, int num_sms, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const size_t n8 = (size_t)T * kHidden / 8;
+  size_t grid = (n8 + 255) / 256;
+  if (grid > (size_t)num_sms * 8) grid = (size_t)num_sms * 8;
+  finalize_kernel<<<(unsigned)grid, 256, 0, st>>>(acc, out, n8);
+  return cudaGetLastError();
+}
+
+}  // namespace moe
