@@ -58,6 +58,14 @@ typedef struct MoeFp8Args {
  */
 int moe_fp8_block_scale_run(const MoeFp8Args* args, void* stream);
 
+/* Launches one stage of moe_fp8_block_scale_run on its own: 0 routing,
+ * 1 permute, 2 GEMM1+SwiGLU, 3 GEMM2+combine, 4 fp32 -> bf16 output. Each stage
+ * reads what the earlier stages left in the workspace, so a stage can be
+ * re-run and timed alone after one full call with the same arguments (GEMM2
+ * adds into the accumulator that stage 0 clears). A profiling aid; the
+ * reference's stages are the separate launches of solution/cuda/pure_moe.cu:589-661. */
+int moe_fp8_run_stage(const MoeFp8Args* args, int32_t stage, void* stream);
+
 /* Workspace bytes for up to `max_tokens` tokens and `num_local_experts` experts.
  * The reference keeps an equivalent op-owned cache (solution/cuda/kernel.cu:25-56,
  * solution/triton/current_kernel.py:186-208); here the caller owns it. */

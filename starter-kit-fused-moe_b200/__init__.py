@@ -65,7 +65,7 @@ class MoeFp8WorkspaceView(ctypes.Structure):
 
 EXPORTED_SYMBOLS = (
     "moe_fp8_block_scale_run", "moe_fp8_workspace_bytes", "moe_fp8_route", "moe_fp8_workspace_view",
-    "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call",
+    "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
 )
 
 _lib = None
@@ -85,6 +85,8 @@ def load_library(path: str | pathlib.Path | None = None) -> ctypes.CDLL:
         vp, i32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
         lib.moe_fp8_block_scale_run.argtypes = [ctypes.POINTER(MoeFp8Args), vp]
         lib.moe_fp8_block_scale_run.restype = ctypes.c_int
+        lib.moe_fp8_run_stage.argtypes = [ctypes.POINTER(MoeFp8Args), i32, vp]
+        lib.moe_fp8_run_stage.restype = ctypes.c_int
         lib.moe_fp8_workspace_bytes.argtypes = [i32, i32]
         lib.moe_fp8_workspace_bytes.restype = sz
         lib.moe_fp8_route.argtypes = [vp, vp, i32, i32, i32, ctypes.c_float, vp, sz, vp]

@@ -143,7 +143,21 @@ int moe_fp8_route(const float* logits, const void* bias, int32_t T, int32_t offs
   return MOE_OK;
 }
 
-int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Everything one call needs: validated arguments, workspace carve-up, TMA maps.
+struct Plan {
+  const MoeFp8Args* a;
+  moe::WsLayout L;
+  int nsm;
+  int* counts; int* topk_idx; float* topk_w; int* pair_pos; int* row_token; float* row_weight;
+  uint8_t* a1; float* sa1; uint8_t* a2; float* sa2; float* acc; int* err;
+  CUtensorMap tmA1, tmB1, tmA2, tmB2;
+};
+
+int make_plan(const MoeFp8Args* a, Plan& p) {
   if (!a) return fail(MOE_ERR_INVALID_ARGUMENT, "args is NULL");
   const int T = a->num_tokens, E = a->num_local_experts;
   if (T < 0) return fail(MOE_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
@@ -159,70 +173,108 @@ int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
       !aligned(a->gemm1_weights_scale, 4) || !aligned(a->gemm2_weights_scale, 4))
     return fail(MOE_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned (scales 4-byte)");
   if (int rc = check_workspace(a->workspace, a->workspace_bytes, T, E)) return rc;
-
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int nsm = num_sms_of_current_device();
-  const moe::WsLayout L = moe::ws_layout(T, E);
+  p.a = a;
+  p.nsm = num_sms_of_current_device();
+  p.L = moe::ws_layout(T, E);
+  const moe::WsLayout& L = p.L;
   uint8_t* w = static_cast<uint8_t*>(a->workspace);
-  int* counts = reinterpret_cast<int*>(w + L.counts);
-  int* topk_idx = reinterpret_cast<int*>(w + L.topk_idx);
-  float* topk_w = reinterpret_cast<float*>(w + L.topk_w);
-  int* pair_pos = reinterpret_cast<int*>(w + L.pair_pos);
-  int* row_token = reinterpret_cast<int*>(w + L.row_token);
-  float* row_weight = reinterpret_cast<float*>(w + L.row_weight);
-  uint8_t* a1 = w + L.a1;
-  float* sa1 = reinterpret_cast<float*>(w + L.sa1);
-  uint8_t* a2 = w + L.a2;
-  float* sa2 = reinterpret_cast<float*>(w + L.sa2);
-  float* acc = reinterpret_cast<float*>(w + L.out_acc);
-  int* err = reinterpret_cast<int*>(w + L.err);
-
-  CUtensorMap tmA1, tmB1, tmA2, tmB2;
-  if (!encode_fp8_2d(&tmA1, a1, moe::kHidden, L.R1, 128) ||
-      !encode_fp8_2d(&tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128) ||
-      !encode_fp8_2d(&tmA2, a2, moe::kInter, 2ull * L.R1, 128) ||
-      !encode_fp8_2d(&tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, 256))
+  p.counts = reinterpret_cast<int*>(w + L.counts);
+  p.topk_idx = reinterpret_cast<int*>(w + L.topk_idx);
+  p.topk_w = reinterpret_cast<float*>(w + L.topk_w);
+  p.pair_pos = reinterpret_cast<int*>(w + L.pair_pos);
+  p.row_token = reinterpret_cast<int*>(w + L.row_token);
+  p.row_weight = reinterpret_cast<float*>(w + L.row_weight);
+  p.a1 = w + L.a1;
+  p.sa1 = reinterpret_cast<float*>(w + L.sa1);
+  p.a2 = w + L.a2;
+  p.sa2 = reinterpret_cast<float*>(w + L.sa2);
+  p.acc = reinterpret_cast<float*>(w + L.out_acc);
+  p.err = reinterpret_cast<int*>(w + L.err);
+  if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, 128) ||
+      !encode_fp8_2d(&p.tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128) ||
+      !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, 128) ||
+      !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, 256))
     return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-
-  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st);
-  if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
-  e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
-                        a->local_expert_offset, E, a->routed_scaling_factor, topk_idx, topk_w, pair_pos, counts, acc,
-                        st);
-  if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
-  e = moe::launch_permute(static_cast<const uint8_t*>(a->hidden_states), a->hidden_states_scale, T, E,
-                          a->local_expert_offset, topk_idx, topk_w, pair_pos, counts, L.R1, a1, sa1, row_token,
-                          row_weight, nsm, st);
-  if (e != cudaSuccess) return cuda_fail(e, "permute kernel launch");
-
-  moe::GemmArgs g1{};
-  g1.counts = counts;
-  g1.E = E;
-  g1.R1 = L.R1;
-  g1.sa = sa1;
-  g1.sb = a->gemm1_weights_scale;
-  g1.a2 = a2;
-  g1.sa2 = sa2;
-  g1.err = err;
-  e = moe::launch_gemm1(tmA1, tmB1, g1, nsm, st);
-  if (e != cudaSuccess) return cuda_fail(e, "GEMM1 launch");
-
-  moe::GemmArgs g2{};
-  g2.counts = counts;
-  g2.E = E;
-  g2.R1 = L.R1;
-  g2.sa = sa2;
-  g2.sb = a->gemm2_weights_scale;
-  g2.row_token = row_token;
-  g2.row_weight = row_weight;
-  g2.out_acc = acc;
-  g2.err = err;
-  e = moe::launch_gemm2(tmA2, tmB2, g2, nsm, st);
-  if (e != cudaSuccess) return cuda_fail(e, "GEMM2 launch");
-
-  e = moe::launch_finalize(acc, static_cast<__nv_bfloat16*>(a->output), T, nsm, st);
-  if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
   return MOE_OK;
+}
+
+int launch_stage(const Plan& p, int stage, cudaStream_t st) {
+  const MoeFp8Args* a = p.a;
+  const int T = a->num_tokens, E = a->num_local_experts;
+  cudaError_t e = cudaSuccess;
+  switch (stage) {
+    case 0:
+      e = cudaMemsetAsync(p.counts, 0, sizeof(int32_t) * E, st);
+      if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
+      e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
+                            a->local_expert_offset, E, a->routed_scaling_factor, p.topk_idx, p.topk_w, p.pair_pos,
+                            p.counts, p.acc, st);
+      if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
+      break;
+    case 1:
+      e = moe::launch_permute(static_cast<const uint8_t*>(a->hidden_states), a->hidden_states_scale, T, E,
+                              a->local_expert_offset, p.topk_idx, p.topk_w, p.pair_pos, p.counts, p.L.R1, p.a1,
+                              p.sa1, p.row_token, p.row_weight, p.nsm, st);
+      if (e != cudaSuccess) return cuda_fail(e, "permute kernel launch");
+      break;
+    case 2: {
+      moe::GemmArgs g{};
+      g.counts = p.counts;
+      g.E = E;
+      g.R1 = p.L.R1;
+      g.sa = p.sa1;
+      g.sb = a->gemm1_weights_scale;
+      g.a2 = p.a2;
+      g.sa2 = p.sa2;
+      g.err = p.err;
+      e = moe::launch_gemm1(p.tmA1, p.tmB1, g, p.nsm, st);
+      if (e != cudaSuccess) return cuda_fail(e, "GEMM1 launch");
+      break;
+    }
+    case 3: {
+      moe::GemmArgs g{};
+      g.counts = p.counts;
+      g.E = E;
+      g.R1 = p.L.R1;
+      g.sa = p.sa2;
+      g.sb = a->gemm2_weights_scale;
+      g.row_token = p.row_token;
+      g.row_weight = p.row_weight;
+      g.out_acc = p.acc;
+      g.err = p.err;
+      e = moe::launch_gemm2(p.tmA2, p.tmB2, g, p.nsm, st);
+      if (e != cudaSuccess) return cuda_fail(e, "GEMM2 launch");
+      break;
+    }
+    case 4:
+      e = moe::launch_finalize(p.acc, static_cast<__nv_bfloat16*>(a->output), T, p.nsm, st);
+      if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
+      break;
+    default:
+      return fail(MOE_ERR_INVALID_ARGUMENT, "stage must be in [0, 4]");
+  }
+  return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
+  Plan p{};
+  if (int rc = make_plan(a, p)) return rc;
+  if (a->num_tokens == 0) return MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int stage = 0; stage < 5; ++stage)
+    if (int rc = launch_stage(p, stage, st)) return rc;
+  return MOE_OK;
+}
+
+int moe_fp8_run_stage(const MoeFp8Args* a, int32_t stage, void* stream) {
+  Plan p{};
+  if (int rc = make_plan(a, p)) return rc;
+  if (a->num_tokens == 0) return MOE_OK;
+  return launch_stage(p, stage, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
