@@ -41,6 +41,7 @@ constexpr int STAGE_BYTES = A_TILE + B_TILE;
 constexpr int GEMM_THREADS = 320;
 constexpr int EPI_WARPS = 8;
 constexpr int TMEM_COLS = 512;
+constexpr int kScalePrefetch = 2;
 
 struct GemmSmem {
   uint64_t full[STAGES];
@@ -59,6 +60,17 @@ struct GemmSmem {
   float amax_x[2][2][BM];
 };
 constexpr size_t GEMM_SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(GemmSmem);
+
+// Optional timeline of CTA 0 (clock64 per K-block and role), enabled by
+// moe_fp8_set_trace(1); slots: 0 promotion wait start, 1 wait end, 2 promotion
+// end, 3 MMA wait start, 4 MMA issued, 5 producer slot acquired.
+constexpr int kTraceKBlocks = 512;
+__device__ unsigned long long g_trace[kTraceKBlocks * 8];
+__device__ int g_trace_on;
+
+__device__ __forceinline__ void trace_mark(int kt, int slot) {
+  if (blockIdx.x == 0 && kt < kTraceKBlocks && g_trace_on) g_trace[kt * 8 + slot] = clock64();
+}
 
 template <int MODE>
 struct GemmCfg;
@@ -206,6 +218,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             ok = false;
             break;
           }
+          trace_mark(it, 5);
           const uint32_t fb = smem_u32(&S.full[s]);
           const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_TILE;
@@ -230,6 +243,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int kb = 0; kb < KB; ++kb, ++it, ++kt) {
           const int s = it % STAGES, u = it / STAGES;
           const int b = kt & 1, v = kt >> 1;
+          trace_mark(kt, 3);
           if (!mbar_wait(smem_u32(&S.tempty[b]), (v & 1) ^ 1) || !mbar_wait(smem_u32(&S.full[s]), u & 1)) {
             set_abort(S, args.err, kErrTimeoutMma);
             ok = false;
@@ -244,6 +258,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mma_e4m3(d, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc, kk > 0 ? 1u : 0u);
           mma_commit(smem_u32(&S.empty[s]));
           mma_commit(smem_u32(&S.tfull[b]));
+          trace_mark(kt, 4);
         }
       }
     }
@@ -274,45 +289,60 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
-      float sa_next = __ldg(args.sa + arow);
-      float sb_next = __ldg(sbp);
-      float sb2_next = MODE == 1 ? __ldg(sbp2) : 0.f;
+      // Block scales are prefetched kScalePrefetch K-blocks ahead in a register
+      // ring, so no global-load latency sits on the per-K-block critical path.
+      constexpr int PF = kScalePrefetch;
+      static_assert(KB % PF == 0, "K-blocks must be a multiple of the prefetch depth");
+      float sa_r[PF], sb_r[PF], sb2_r[PF];
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        sa_r[u] = __ldg(args.sa + (size_t)u * ld_sa + arow);
+        sb_r[u] = __ldg(sbp + u);
+        sb2_r[u] = MODE == 1 ? __ldg(sbp2 + u) : 0.f;
+      }
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb, ++kt) {
-        const float sa_cur = sa_next, sb_cur = sb_next, sb2_cur = sb2_next;
-        if (kb + 1 < KB) {
-          sa_next = __ldg(args.sa + (size_t)(kb + 1) * ld_sa + arow);
-          sb_next = __ldg(sbp + kb + 1);
-          if (MODE == 1) sb2_next = __ldg(sbp2 + kb + 1);
-        }
-        const int b = kt & 1, v = kt >> 1;
-        if (!mbar_wait(smem_u32(&S.tfull[b]), v & 1)) {
-          set_abort(S, args.err, kErrTimeoutEpilogue);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t base = lane_addr + (uint32_t)(b * BN);
-        const float f0 = sa_cur * sb_cur;
-        const float f1 = MODE == 1 ? sa_cur * sb2_cur : f0;
+      for (int kb0 = 0; kb0 < KB && ok; kb0 += PF) {
 #pragma unroll
-        for (int c = 0; c < 8; c += 2) {
-          // MODE 1: chunks 0-3 = gate columns 64g.., chunks 4-7 = up columns 128+64g..
-          const int col0 = MODE == 1 ? (c < 4 ? 64 * g + 16 * c : 128 + 64 * g + 16 * (c - 4)) : 128 * g + 16 * c;
-          float p0[16], p1[16];
-          tmem_ld16(base + col0, p0);
-          tmem_ld16(base + col0 + 16, p1);
-          tmem_ld_wait();
-          const float f = c < 4 ? f0 : f1;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            acc[16 * c + i] = fmaf(p0[i], f, acc[16 * c + i]);
-            acc[16 * c + 16 + i] = fmaf(p1[i], f, acc[16 * c + 16 + i]);
+        for (int u = 0; u < PF; ++u) {
+          const int kb = kb0 + u;
+          const float f0 = sa_r[u] * sb_r[u];
+          const float f1 = MODE == 1 ? sa_r[u] * sb2_r[u] : f0;
+          if (kb + PF < KB) {
+            sa_r[u] = __ldg(args.sa + (size_t)(kb + PF) * ld_sa + arow);
+            sb_r[u] = __ldg(sbp + kb + PF);
+            if (MODE == 1) sb2_r[u] = __ldg(sbp2 + kb + PF);
           }
+          const int b = kt & 1, v = kt >> 1;
+          if (warp == 4 && lane == 0) trace_mark(kt, 0);
+          if (!mbar_wait(smem_u32(&S.tfull[b]), v & 1)) {
+            set_abort(S, args.err, kErrTimeoutEpilogue);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (warp == 4 && lane == 0) trace_mark(kt, 1);
+          const uint32_t base = lane_addr + (uint32_t)(b * BN);
+#pragma unroll
+          for (int c = 0; c < 8; c += 2) {
+            // MODE 1: chunks 0-3 = gate columns 64g.., chunks 4-7 = up columns 128+64g..
+            const int col0 = MODE == 1 ? (c < 4 ? 64 * g + 16 * c : 128 + 64 * g + 16 * (c - 4)) : 128 * g + 16 * c;
+            float p0[16], p1[16];
+            tmem_ld16(base + col0, p0);
+            tmem_ld16(base + col0 + 16, p1);
+            tmem_ld_wait();
+            const float f = c < 4 ? f0 : f1;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              acc[16 * c + i] = fmaf(p0[i], f, acc[16 * c + i]);
+              acc[16 * c + 16 + i] = fmaf(p1[i], f, acc[16 * c + 16 + i]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&S.tempty[b]));
+          if (warp == 4 && lane == 0) trace_mark(kt, 2);
+          ++kt;
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&S.tempty[b]));
       }
       if (!ok) break;
 
@@ -420,6 +450,19 @@ cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
   }
   grouped_gemm_kernel<MODE><<<num_sms, GEMM_THREADS, GEMM_SMEM_BYTES, st>>>(tmA, tmB, args);
   return cudaGetLastError();
+}
+
+cudaError_t set_trace(int on) {
+  cudaError_t e = cudaMemcpyToSymbol(g_trace_on, &on, sizeof(int));
+  if (e == cudaSuccess && on) {
+    static unsigned long long zeros[kTraceKBlocks * 8];
+    e = cudaMemcpyToSymbol(g_trace, zeros, sizeof(zeros));
+  }
+  return e;
+}
+cudaError_t read_trace(unsigned long long* host, int n) {
+  if (n > kTraceKBlocks * 8) n = kTraceKBlocks * 8;
+  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * n);
 }
 
 cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,

@@ -7,6 +7,7 @@
 // per-expert histogram stays on the device and the GEMM kernels build their
 // tile lists from it.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -268,6 +269,12 @@ int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
   for (int stage = 0; stage < 5; ++stage)
     if (int rc = launch_stage(p, stage, st)) return rc;
   return MOE_OK;
+}
+
+// Profiling aid: timeline of the GEMM kernels' CTA 0 (see grouped_gemm.cu).
+int moe_fp8_debug_trace(int32_t enable, uint64_t* host, int32_t n) {
+  cudaError_t e = enable >= 0 ? moe::set_trace(enable) : moe::read_trace(reinterpret_cast<unsigned long long*>(host), n);
+  return e == cudaSuccess ? MOE_OK : cuda_fail(e, "trace");
 }
 
 int moe_fp8_run_stage(const MoeFp8Args* a, int32_t stage, void* stream) {

@@ -14,13 +14,21 @@
 
 namespace moe {
 
-constexpr int kRouteWarps = 8;
-constexpr int kRouteTokensPerWarp = 4;
-constexpr int kRouteTokensPerBlock = kRouteWarps * kRouteTokensPerWarp;
+constexpr int kRouteWarps = 8;   // one token per warp, 8 tokens per block
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// Order-preserving map of a float onto uint32 (larger float -> larger key);
+// key 0 is below every finite value and marks removed / masked experts.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 // One warp per token; lane l owns experts 8l..8l+7, so lanes 4g..4g+3 hold group g.
+// Each of the 8 selection rounds is one warp max-reduction (redux.sync) of the
+// lanes' best keys plus a ballot for the lowest lane holding that key, so
+// exact ties resolve to the lower expert index.
 // Local selections are counted per block in shared memory and published with
 // one global atomic per (block, expert); each selection gets its position
 // inside its expert's group (pair_pos), -1 when the expert is not local.
@@ -32,34 +40,28 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
   __shared__ int base[kMaxLocalExperts];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-
-  int my_le[kRouteTokensPerWarp], my_lpos[kRouteTokensPerWarp];
-#pragma unroll
-  for (int i = 0; i < kRouteTokensPerWarp; ++i) {
-    my_le[i] = -1;
-    my_lpos[i] = 0;
-    const int t = blockIdx.x * kRouteTokensPerBlock + warp * kRouteTokensPerWarp + i;
-    if (t >= T) continue;  // warp-uniform
+  const int t = blockIdx.x * kRouteWarps + warp;
+  const bool active = t < T;  // warp-uniform
+  float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+  uint4 braw = make_uint4(0, 0, 0, 0);
+  if (active) {
     const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExperts + lane * 8);
-    const float4 x0 = __ldg(lp), x1 = __ldg(lp + 1);
+    x0 = __ldg(lp);
+    x1 = __ldg(lp + 1);
+    if (bias != nullptr) braw = __ldg(reinterpret_cast<const uint4*>(bias + lane * 8));
+  }
+  __syncthreads();
+  int my_le = -1, my_lpos = 0;
+  if (active) {
     const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-    float b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (bias != nullptr) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(bias + lane * 8));
-      const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(bp[j]);
-        b[2 * j] = f.x;
-        b[2 * j + 1] = f.y;
-      }
-    }
-    float sb[8];
+    const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&braw);
+    float s[8], sb[8];
     float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      sb[j] = sigmoid_ref(x[j]) + b[j];
+      const float2 bf = __bfloat1622float2(bp[j >> 1]);
+      s[j] = sigmoid_ref(x[j]);
+      sb[j] = s[j] + ((j & 1) ? bf.y : bf.x);
       if (sb[j] > m1) {
         m2 = m1;
         m1 = sb[j];
@@ -72,9 +74,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
     for (int d = 1; d <= 2; d <<= 1) {
       const float o1 = __shfl_xor_sync(0xffffffffu, m1, d);
       const float o2 = __shfl_xor_sync(0xffffffffu, m2, d);
-      const float n1 = fmaxf(m1, o1);
       const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
-      m1 = n1;
+      m1 = fmaxf(m1, o1);
       m2 = n2;
     }
     const float gscore = m1 + m2;
@@ -86,35 +87,41 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
       rank += (gs > gscore) || (gs == gscore && g < mygroup);
     }
     const bool keep = rank < kTopKGroups;
+    uint32_t key[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) key[j] = keep ? order_key(sb[j]) : 0u;
 
-    // 8 rounds of warp argmax over the kept experts (ties -> lower index)
-    uint32_t removed = keep ? 0u : 0xffu;
     int sel = 0;
+    float s_sel = 0.f;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
+      uint32_t lk = 0;
+      int lj = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (!((removed >> j) & 1u) && (bi == 0x7fffffff || sb[j] > bv)) {
-          bv = sb[j];
-          bi = lane * 8 + j;
+      for (int j = 0; j < 8; ++j)
+        if (key[j] > lk) {
+          lk = key[j];
+          lj = j;
         }
-      }
+      const uint32_t m = __reduce_max_sync(0xffffffffu, lk);
+      const int wl = __ffs(__ballot_sync(0xffffffffu, lk == m)) - 1;
+      const int wj = __shfl_sync(0xffffffffu, lj, wl);
+      float ws = 0.f;
 #pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
-        if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) {
-          bv = ov;
-          bi = oi;
-        }
+      for (int j = 0; j < 8; ++j)
+        if (j == wj) ws = s[j];
+      ws = __shfl_sync(0xffffffffu, ws, wl);
+      if (lane == wl) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j == wj) key[j] = 0u;
       }
-      if ((bi >> 3) == lane) removed |= 1u << (bi & 7);
-      if (lane == k) sel = bi;
+      if (lane == k) {
+        sel = wl * 8 + wj;
+        s_sel = ws;
+      }
     }
-    // combine weights from the un-biased sigmoid (recomputed: same input, same value)
-    const float s_sel = lane < kTopK ? sigmoid_ref(__ldg(logits + (size_t)t * kExperts + sel)) : 0.f;
+    // combine weights from the un-biased sigmoid, summed in selection order
     float sum = 0.f;
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) sum += __shfl_sync(0xffffffffu, s_sel, k);
@@ -124,25 +131,22 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
       topk_w[(size_t)t * kTopK + lane] = w;
       const int le = sel - offset;
       if (le >= 0 && le < E) {
-        my_le[i] = le;
-        my_lpos[i] = atomicAdd(&hist[le], 1);
+        my_le = le;
+        my_lpos = atomicAdd(&hist[le], 1);
       }
     }
     // clear this token's combine accumulator row
     if (out_acc != nullptr) {
       float4* row = reinterpret_cast<float4*>(out_acc + (size_t)t * kHidden);
       const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
       for (int c = lane; c < kHidden / 4; c += 32) row[c] = z;
     }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] = hist[e] ? atomicAdd(&counts[e], hist[e]) : 0;
   __syncthreads();
-#pragma unroll
-  for (int i = 0; i < kRouteTokensPerWarp; ++i) {
-    const int t = blockIdx.x * kRouteTokensPerBlock + warp * kRouteTokensPerWarp + i;
-    if (t < T && lane < kTopK) pair_pos[(size_t)t * kTopK + lane] = my_le[i] >= 0 ? base[my_le[i]] + my_lpos[i] : -1;
-  }
+  if (active && lane < kTopK) pair_pos[(size_t)t * kTopK + lane] = my_le >= 0 ? base[my_le] + my_lpos : -1;
 }
 
 // Exclusive scan of align_up(counts[e], 128) over e < E (E <= 256) into off[];
@@ -232,7 +236,7 @@ cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, 
                          int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
                          cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  const int grid = (T + kRouteTokensPerBlock - 1) / kRouteTokensPerBlock;
+  const int grid = (T + kRouteWarps - 1) / kRouteWarps;
   route_kernel<<<grid, kRouteWarps * 32, 0, st>>>(logits, bias, T, offset, E, scale, topk_idx, topk_w, pair_pos,
                                                   counts, out_acc);
   return cudaGetLastError();
