@@ -34,6 +34,9 @@ W13_BYTES = 2 * I * H + 32 * 56 * 4                          # per expert, with 
 W2_BYTES = H * I + 56 * 16 * 4
 TOKEN_IO_BYTES = 256 * 4 + H + 56 * 4 + H * 2                # logits, hidden, scales, bf16 output
 L2_FLUSH_BYTES = 256 << 20
+# dram__bytes_read.sum + dram__bytes_write.sum of one GEMM1 launch at the default
+# workload (T=64, seed 0), from profiles/swap_gemm_kernel_decode_T64.md
+GEMM1_TRAFFIC_BYTES = {64: 505_836_032}
 
 
 def load_peaks():
@@ -313,11 +316,11 @@ def main():
                    "l2": "flushed (256 MB write) between timed calls; weights also exceed L2"},
         "tflops": pairs * FLOPS_PER_PAIR / (ms_per_step * 1e-3) / 1e12,
         "hbm_gbs_whole_call": algorithmic_bytes(T, pairs, hit) / (ms_per_step * 1e-3) / 1e9,
-        "roofline": {"kernel": "grouped_gemm_kernel<1> (GEMM1+SwiGLU)", "bound": "hbm",
+        "roofline": {"kernel": ("swap_gemm_kernel<1>" if T <= pkg.set_decode_max_tokens(-1) else "grouped_gemm_kernel<1>") + " (GEMM1+SwiGLU)", "bound": "hbm",
                      "achieved": g1_achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": g1_achieved / hbm_peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": g1_bytes, "launch_us": g1_ms * 1e3,
-                     "traffic": None},
+                     "traffic": GEMM1_TRAFFIC_BYTES.get(T) if rank == 0 else None},
         "e2e": {"value": e2e_ms * 1e3, "unit": "us", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": a.steps * int(pkg.load_library().moe_fp8_kernels_per_call(T)),
         "clocks": clk.summary(),

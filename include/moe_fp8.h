@@ -66,6 +66,15 @@ int moe_fp8_block_scale_run(const MoeFp8Args* args, void* stream);
  * reference's stages are the separate launches of solution/cuda/pure_moe.cu:589-661. */
 int moe_fp8_run_stage(const MoeFp8Args* args, int32_t stage, void* stream);
 
+/* Calls with at most `max_tokens` tokens use the weight-streaming GEMM
+ * kernels (weights on the MMA's M side, 16 tokens per tile); larger calls use
+ * the 128-token-row tile kernels. Sets the threshold of both GEMMs (defaults:
+ * 256 for GEMM1, 96 for GEMM2, or $MOE_DECODE_MAX_TOKENS for both). A negative
+ * value only queries. Returns the previous GEMM1 threshold. Plays the
+ * role of the reference's token-count path selection
+ * (solution/triton/current_kernel.py:1812-1813, :2022). */
+int32_t moe_fp8_set_decode_max_tokens(int32_t max_tokens);
+
 /* Workspace bytes for up to `max_tokens` tokens and `num_local_experts` experts.
  * The reference keeps an equivalent op-owned cache (solution/cuda/kernel.cu:25-56,
  * solution/triton/current_kernel.py:186-208); here the caller owns it. */

@@ -66,6 +66,7 @@ class MoeFp8WorkspaceView(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "moe_fp8_block_scale_run", "moe_fp8_workspace_bytes", "moe_fp8_route", "moe_fp8_workspace_view",
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
+    "moe_fp8_set_decode_max_tokens",
 )
 
 _lib = None
@@ -97,6 +98,10 @@ def load_library(path: str | pathlib.Path | None = None) -> ctypes.CDLL:
         lib.moe_fp8_read_device_error.restype = ctypes.c_int
         lib.moe_fp8_last_error.argtypes = []
         lib.moe_fp8_last_error.restype = ctypes.c_char_p
+        lib.moe_fp8_set_decode_max_tokens.argtypes = [i32]
+        lib.moe_fp8_set_decode_max_tokens.restype = i32
+        lib.moe_fp8_debug_trace.argtypes = [i32, vp, i32]
+        lib.moe_fp8_debug_trace.restype = ctypes.c_int
         lib.moe_fp8_kernels_per_call.argtypes = [i32]
         lib.moe_fp8_kernels_per_call.restype = i32
         if path is None:
@@ -252,6 +257,11 @@ def workspace_tensors(ws: torch.Tensor, T: int, E: int):
     return (view(v.topk_idx, T * TOP_K, torch.int32).view(T, TOP_K),
             view(v.topk_weights, T * TOP_K, torch.float32).view(T, TOP_K),
             view(v.expert_counts, E, torch.int32))
+
+
+def set_decode_max_tokens(max_tokens: int) -> int:
+    """Token-count threshold for the weight-streaming GEMM kernels; returns the previous one."""
+    return int(load_library().moe_fp8_set_decode_max_tokens(int(max_tokens)))
 
 
 def read_device_error(device=None) -> int:

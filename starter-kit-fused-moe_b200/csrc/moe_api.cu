@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -156,7 +157,22 @@ struct Plan {
   int* counts; int* topk_idx; float* topk_w; int* pair_pos; int* row_token; float* row_weight;
   uint8_t* a1; float* sa1; uint8_t* a2; float* sa2; float* acc; int* err;
   CUtensorMap tmA1, tmB1, tmA2, tmB2;
+  bool decode1, decode2;  // weight-streaming (swap-AB) GEMM1 / GEMM2 kernels
 };
+
+// Calls with at most this many tokens use the decode-shaped GEMM kernels
+// (few tokens per expert; weights on the MMA's M side). Measured crossovers on B200: the weight-streaming GEMM1 wins up to a few
+// hundred tokens, the weight-streaming GEMM2 only up to about a hundred.
+std::atomic<int> g_decode_max_tokens[2] = {{-1}, {-1}};
+int decode_max_tokens(int which) {
+  int v = g_decode_max_tokens[which].load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = getenv("MOE_DECODE_MAX_TOKENS");
+    v = e ? atoi(e) : (which == 0 ? 256 : 96);
+    g_decode_max_tokens[which].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
 
 int make_plan(const MoeFp8Args* a, Plan& p) {
   if (!a) return fail(MOE_ERR_INVALID_ARGUMENT, "args is NULL");
@@ -170,9 +186,9 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
     return fail(MOE_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
   if (!aligned(a->routing_logits, 16) || !aligned(a->hidden_states, 16) || !aligned(a->gemm1_weights, 16) ||
       !aligned(a->gemm2_weights, 16) || !aligned(a->output, 16) ||
-      (a->routing_bias && !aligned(a->routing_bias, 16)) || !aligned(a->hidden_states_scale, 4) ||
-      !aligned(a->gemm1_weights_scale, 4) || !aligned(a->gemm2_weights_scale, 4))
-    return fail(MOE_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned (scales 4-byte)");
+      (a->routing_bias && !aligned(a->routing_bias, 16)) || !aligned(a->hidden_states_scale, 16) ||
+      !aligned(a->gemm1_weights_scale, 16) || !aligned(a->gemm2_weights_scale, 16))
+    return fail(MOE_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
   if (int rc = check_workspace(a->workspace, a->workspace_bytes, T, E)) return rc;
   p.a = a;
   p.nsm = num_sms_of_current_device();
@@ -191,10 +207,13 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
   p.sa2 = reinterpret_cast<float*>(w + L.sa2);
   p.acc = reinterpret_cast<float*>(w + L.out_acc);
   p.err = reinterpret_cast<int*>(w + L.err);
-  if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, 128) ||
+  p.decode1 = T <= decode_max_tokens(0);
+  p.decode2 = T <= decode_max_tokens(1);
+  const uint32_t w2_box = p.decode2 ? 128 : 256;
+  if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, p.decode1 ? 16 : 128) ||
       !encode_fp8_2d(&p.tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128) ||
-      !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, 128) ||
-      !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, 256))
+      !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, p.decode2 ? 16 : 128) ||
+      !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, w2_box))
     return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   return MOE_OK;
 }
@@ -228,7 +247,8 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       g.a2 = p.a2;
       g.sa2 = p.sa2;
       g.err = p.err;
-      e = moe::launch_gemm1(p.tmA1, p.tmB1, g, p.nsm, st);
+      e = p.decode1 ? moe::launch_gemm1_decode(p.tmA1, p.tmB1, g, p.nsm, st)
+                   : moe::launch_gemm1(p.tmA1, p.tmB1, g, p.nsm, st);
       if (e != cudaSuccess) return cuda_fail(e, "GEMM1 launch");
       break;
     }
@@ -243,7 +263,8 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       g.row_weight = p.row_weight;
       g.out_acc = p.acc;
       g.err = p.err;
-      e = moe::launch_gemm2(p.tmA2, p.tmB2, g, p.nsm, st);
+      e = p.decode2 ? moe::launch_gemm2_decode(p.tmA2, p.tmB2, g, p.nsm, st)
+                   : moe::launch_gemm2(p.tmA2, p.tmB2, g, p.nsm, st);
       if (e != cudaSuccess) return cuda_fail(e, "GEMM2 launch");
       break;
     }
@@ -269,6 +290,15 @@ int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
   for (int stage = 0; stage < 5; ++stage)
     if (int rc = launch_stage(p, stage, st)) return rc;
   return MOE_OK;
+}
+
+int32_t moe_fp8_set_decode_max_tokens(int32_t max_tokens) {
+  const int32_t old = decode_max_tokens(0);
+  if (max_tokens >= 0) {
+    g_decode_max_tokens[0].store(max_tokens, std::memory_order_relaxed);
+    g_decode_max_tokens[1].store(max_tokens, std::memory_order_relaxed);
+  }
+  return old;
 }
 
 // Profiling aid: timeline of the GEMM kernels' CTA 0 (see grouped_gemm.cu).

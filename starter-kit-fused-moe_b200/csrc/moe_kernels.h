@@ -28,6 +28,10 @@ cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E,
                            const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
                            float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st);
 cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, int num_sms, cudaStream_t st);
+cudaError_t launch_gemm1_decode(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& args,
+                                int num_sms, cudaStream_t st);
+cudaError_t launch_gemm2_decode(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& args,
+                                int num_sms, cudaStream_t st);
 cudaError_t set_trace(int on);
 cudaError_t read_trace(unsigned long long* host, int n);
 cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,

@@ -76,22 +76,42 @@ def gpu_inputs(pkg):
     torch.cuda.empty_cache()
 
 
+@pytest.fixture(params=["decode", "tiles"])
+def kernel_path(request, pkg):
+    """Run a test through the weight-streaming kernels or the 128-row tile kernels."""
+    old = pkg.set_decode_max_tokens(1 << 30 if request.param == "decode" else 0)
+    yield request.param
+    pkg.set_decode_max_tokens(old)
+
+
 @pytest.mark.parametrize("T", [2, 17, 64, 200])
-def test_output_matches_oracle(T, pkg, oracle, gpu_inputs):
+def test_output_matches_oracle(T, kernel_path, pkg, oracle, gpu_inputs):
     x = gpu_inputs(T, seed=100 + T)
     out = pkg.run(*x.args())
+    torch.cuda.synchronize()
+    assert pkg.read_device_error() == 0
     ref = oracle.moe_forward(*x.args())
-    err = assert_close(out.float().cpu().numpy(), ref, what=f"T={T}")
-    print(f"T={T}: max_abs_err={err:.3e}")
+    err = assert_close(out.float().cpu().numpy(), ref, what=f"T={T} {kernel_path}")
+    print(f"T={T} {kernel_path}: max_abs_err={err:.3e}")
 
 
-def test_many_tokens_per_expert(pkg, oracle, gpu_inputs):
-    """Skewed routing: experts 0/8/16/24 receive every token, several 128-row tiles each."""
+def test_many_tokens_per_expert(kernel_path, pkg, oracle, gpu_inputs):
+    """Skewed routing: experts 0/8/16/24 receive every token, several tiles each."""
     x = gpu_inputs(600, seed=7, skewed=True)
     out = pkg.run(*x.args())
     ref = oracle.moe_forward(*x.args())
-    err = assert_close(out.float().cpu().numpy(), ref, what="skewed T=600")
-    print(f"skewed T=600: max_abs_err={err:.3e}")
+    err = assert_close(out.float().cpu().numpy(), ref, what=f"skewed T=600 {kernel_path}")
+    print(f"skewed T=600 {kernel_path}: max_abs_err={err:.3e}")
+
+
+def test_both_paths_agree(pkg, gpu_inputs):
+    x = gpu_inputs(64, seed=31)
+    old = pkg.set_decode_max_tokens(1 << 30)
+    a = pkg.run(*x.args()).float()
+    pkg.set_decode_max_tokens(0)
+    b = pkg.run(*x.args()).float()
+    pkg.set_decode_max_tokens(old)
+    assert torch.allclose(a, b, atol=4e-3, rtol=1e-2)
 
 
 @pytest.mark.parametrize("offset", [32, 224])
