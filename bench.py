@@ -34,9 +34,9 @@ W13_BYTES = 2 * I * H + 32 * 56 * 4                          # per expert, with 
 W2_BYTES = H * I + 56 * 16 * 4
 TOKEN_IO_BYTES = 256 * 4 + H + 56 * 4 + H * 2                # logits, hidden, scales, bf16 output
 L2_FLUSH_BYTES = 256 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one GEMM1 launch at the default
-# workload (T=64, seed 0), from profiles/swap_gemm_kernel_decode_T64.md
-GEMM1_TRAFFIC_BYTES = {64: 505_836_032}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
+# kernel at the default workload (T=64, seed 0), from the ncu summary in profiles/
+GEMM1_TRAFFIC_BYTES = {}
 
 
 def load_peaks():
@@ -49,50 +49,52 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling while the timed region runs."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    ~2 ms while the timed region runs (nvidia-smi as a fallback)."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.samples = []
-        self.proc = None
+        self.samples = []        # (sm_mhz, reasons bitmask)
+        self.max_mhz = None
+        self._stop = threading.Event()
 
     def __enter__(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((sm, rs))
+                    except Exception:
+                        pass
+                    time.sleep(0.002)
+            self.thread = threading.Thread(target=poll, daemon=True)
             self.thread.start()
         except Exception:
-            self.proc = None
+            self.thread = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 7:
-                self.samples.append(parts)
-
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        sm = [s[0] for s in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
 
 
 def dist_setup():
@@ -177,6 +179,11 @@ def gemm1_bytes(pairs, hit):
     return hit * W13_BYTES + pairs * (H + 56 * 4) + pairs * 2 * (I + 16 * 4)
 
 
+def gemm2_bytes(pairs, hit):
+    # W2 tiles of the hit experts + two-term intermediate rows/scales in + fp32 accumulator adds
+    return hit * W2_BYTES + pairs * 2 * (I + 16 * 4) + pairs * H * 4 * 2
+
+
 def cpu_reference_time(pkg, O, x, max_seconds=60.0):
     """Time the oracle (numpy restatement of the definition's reference) on host cores."""
     xc = x.to("cpu")
@@ -239,7 +246,7 @@ def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, n=5, warm=3):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -275,10 +282,17 @@ def main():
     ms_per_step = total_ms / a.steps
     pairs, hit = op.routing_stats()
 
-    # ---- dominant kernel (GEMM1: weight streaming) timed alone, same stream
+    # ---- dominant kernel timed alone on the same stream: the fused weight-streaming
+    # GEMM1+GEMM2 launch (decode sizes) or GEMM1 (larger calls)
+    path = pkg.gemm_path(T)
     g1 = timed(lambda: op.stage(2), a.steps, flush)
     g1_ms = statistics.median(g1)
-    g1_bytes = gemm1_bytes(pairs, hit)
+    if path == 2:
+        kname = "stream_gemm_kernel (GEMM1+SwiGLU+GEMM2+combine, one launch)"
+        g1_bytes = gemm1_bytes(pairs, hit) + gemm2_bytes(pairs, hit)
+    else:
+        kname = ("stream_gemm_kernel" if path in (1, 3) else "grouped_gemm_kernel<1>") + " (GEMM1+SwiGLU)"
+        g1_bytes = gemm1_bytes(pairs, hit)
     g1_achieved = g1_bytes / (g1_ms * 1e-3) / 1e9
 
     # ---- end to end through the public run(...) with host buffers
@@ -316,7 +330,7 @@ def main():
                    "l2": "flushed (256 MB write) between timed calls; weights also exceed L2"},
         "tflops": pairs * FLOPS_PER_PAIR / (ms_per_step * 1e-3) / 1e12,
         "hbm_gbs_whole_call": algorithmic_bytes(T, pairs, hit) / (ms_per_step * 1e-3) / 1e9,
-        "roofline": {"kernel": ("swap_gemm_kernel<1>" if T <= pkg.set_decode_max_tokens(-1) else "grouped_gemm_kernel<1>") + " (GEMM1+SwiGLU)", "bound": "hbm",
+        "roofline": {"kernel": kname, "bound": "hbm",
                      "achieved": g1_achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": g1_achieved / hbm_peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": g1_bytes, "launch_us": g1_ms * 1e3,

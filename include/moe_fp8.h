@@ -62,18 +62,23 @@ int moe_fp8_block_scale_run(const MoeFp8Args* args, void* stream);
  * 1 permute, 2 GEMM1+SwiGLU, 3 GEMM2+combine, 4 fp32 -> bf16 output. Each stage
  * reads what the earlier stages left in the workspace, so a stage can be
  * re-run and timed alone after one full call with the same arguments (GEMM2
- * adds into the accumulator that stage 0 clears). A profiling aid; the
+ * adds into the accumulator that stage 0 clears). With GEMM path 2 stage 2
+ * runs both GEMMs and stage 3 launches nothing. A profiling aid; the
  * reference's stages are the separate launches of solution/cuda/pure_moe.cu:589-661. */
 int moe_fp8_run_stage(const MoeFp8Args* args, int32_t stage, void* stream);
 
-/* Calls with at most `max_tokens` tokens use the weight-streaming GEMM
- * kernels (weights on the MMA's M side, 16 tokens per tile); larger calls use
- * the 128-token-row tile kernels. Sets the threshold of both GEMMs (defaults:
- * 256 for GEMM1, 96 for GEMM2, or $MOE_DECODE_MAX_TOKENS for both). A negative
- * value only queries. Returns the previous GEMM1 threshold. Plays the
- * role of the reference's token-count path selection
- * (solution/triton/current_kernel.py:1812-1813, :2022). */
-int32_t moe_fp8_set_decode_max_tokens(int32_t max_tokens);
+/* GEMM kernel family used for a call with `num_tokens` tokens:
+ *   0  128-row tile kernels for both GEMMs (prefill shapes),
+ *   1  weight-streaming GEMM1 + tile GEMM2,
+ *   2  one weight-streaming launch doing GEMM1 and GEMM2 (decode shapes),
+ *   3  weight-streaming GEMM1 and GEMM2 as two launches.
+ * Automatic choice: 2 up to 384 tokens, 0 above. Plays the role of
+ * the reference's token-count path selection (solution/triton/current_kernel.py:1812-1813, :2022). */
+int32_t moe_fp8_gemm_path(int32_t num_tokens);
+
+/* Forces a GEMM kernel family for every call (0..3), or -1 for the automatic
+ * choice ($MOE_GEMM_PATH sets the initial value). Returns the previous setting. */
+int32_t moe_fp8_set_gemm_path(int32_t path);
 
 /* Workspace bytes for up to `max_tokens` tokens and `num_local_experts` experts.
  * The reference keeps an equivalent op-owned cache (solution/cuda/kernel.cu:25-56,

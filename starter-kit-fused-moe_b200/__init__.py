@@ -66,7 +66,7 @@ class MoeFp8WorkspaceView(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "moe_fp8_block_scale_run", "moe_fp8_workspace_bytes", "moe_fp8_route", "moe_fp8_workspace_view",
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
-    "moe_fp8_set_decode_max_tokens",
+    "moe_fp8_set_gemm_path", "moe_fp8_gemm_path",
 )
 
 _lib = None
@@ -98,8 +98,10 @@ def load_library(path: str | pathlib.Path | None = None) -> ctypes.CDLL:
         lib.moe_fp8_read_device_error.restype = ctypes.c_int
         lib.moe_fp8_last_error.argtypes = []
         lib.moe_fp8_last_error.restype = ctypes.c_char_p
-        lib.moe_fp8_set_decode_max_tokens.argtypes = [i32]
-        lib.moe_fp8_set_decode_max_tokens.restype = i32
+        lib.moe_fp8_set_gemm_path.argtypes = [i32]
+        lib.moe_fp8_set_gemm_path.restype = i32
+        lib.moe_fp8_gemm_path.argtypes = [i32]
+        lib.moe_fp8_gemm_path.restype = i32
         lib.moe_fp8_debug_trace.argtypes = [i32, vp, i32]
         lib.moe_fp8_debug_trace.restype = ctypes.c_int
         lib.moe_fp8_kernels_per_call.argtypes = [i32]
@@ -259,9 +261,18 @@ def workspace_tensors(ws: torch.Tensor, T: int, E: int):
             view(v.expert_counts, E, torch.int32))
 
 
-def set_decode_max_tokens(max_tokens: int) -> int:
-    """Token-count threshold for the weight-streaming GEMM kernels; returns the previous one."""
-    return int(load_library().moe_fp8_set_decode_max_tokens(int(max_tokens)))
+GEMM_PATHS = {0: "tile kernels", 1: "streaming GEMM1 + tile GEMM2", 2: "fused streaming GEMM1+GEMM2",
+              3: "streaming GEMM1 + streaming GEMM2"}
+
+
+def set_gemm_path(path: int) -> int:
+    """Force a GEMM kernel family (0..3, see GEMM_PATHS) or -1 for automatic; returns the previous setting."""
+    return int(load_library().moe_fp8_set_gemm_path(int(path)))
+
+
+def gemm_path(num_tokens: int) -> int:
+    """GEMM kernel family a call with `num_tokens` tokens uses."""
+    return int(load_library().moe_fp8_gemm_path(int(num_tokens)))
 
 
 def read_device_error(device=None) -> int:

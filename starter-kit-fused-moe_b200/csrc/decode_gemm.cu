@@ -5,96 +5,88 @@
 // bytes. These kernels put the weights on the MMA's M side (128 weight rows per
 // instruction) and 16 token rows on N ("swap-AB"):
 //   D[w_row, token] = sum_k W[w_row, k] * A[token, k]
-// so a pipeline stage is almost all weight bytes (2 KB of activations next to
-// 16 or 32 KB of weights) and six to ten stages fit in shared memory, enough
-// bytes in flight for one SM to keep its share of HBM bandwidth busy.
-// Each K-block's 128x16 fp32 partial lands in its own TMEM slot of a 16- or
-// 32-deep ring, so the tensor core runs ahead of the scale promotion instead of
-// handing one buffer back and forth.
+// A pipeline stage holds two 128-row weight blocks (32 KB) and 16 activation
+// rows (2 KB); six stages keep ~200 KB of weights in flight per SM. Each
+// K-block's two 128x16 fp32 partials land in their own 32-column TMEM slot of
+// a 16-deep ring, so the tensor core runs ahead of the scale promotion.
 //
-// GEMM1 (MODE 1): per tile (expert, 128 intermediate columns, 16 pair rows),
-//   two MMAs per K=32 step: gate rows and up rows of W13 against the same
-//   activation rows; promotion by w_scale[row block, kb] * a_scale[token, kb];
-//   epilogue SwiGLU and the two-term FP8 re-quantisation of grouped_gemm.cu
-//   (1x128 blocks = the 128 columns this tile owns), amax reduced across the
-//   tile's 128 threads per token.
-// GEMM2 (MODE 2): per tile (expert, 128 output columns, 16 term rows = 8
-//   pairs); hi + lo terms summed, times the routing weight, added into the fp32
-//   token accumulator (one coalesced 128-byte atomic add per warp and pair).
+// Tiles (all: 16 activation rows, two 128-row weight blocks):
+//   GEMM1 tile (expert, n1 in 0..15, token tile): W13 gate rows [128 n1, +128)
+//     and up rows [2048 + 128 n1, +128); epilogue SwiGLU and the two-term FP8
+//     re-quantisation of grouped_gemm.cu over the 128 columns the tile owns.
+//   GEMM2 tile (expert, n2 in 0..27, term tile of 8 pairs): W2 rows
+//     [256 n2, +256); epilogue sums each pair's hi/lo terms, scales by the
+//     routing weight and adds into the fp32 token accumulator.
+// Tiles come from a device-side queue (one atomic counter per launch), so the
+// work balances across SMs and, in the fused mode, GEMM2 tiles of an expert
+// start as soon as that expert's GEMM1 tiles are done: each GEMM1 tile bumps a
+// per-expert counter after its stores; the producer of a GEMM2 tile waits for
+// the count (bounded), then fences the async proxy before its TMA reads.
+// GEMM1 tiles are queued before all GEMM2 tiles and a CTA only waits on tiles
+// already claimed by running CTAs, so the wait cannot deadlock.
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 
 namespace moe {
 namespace dec {
 
-constexpr int NTOK = 16;                 // token rows per tile (MMA N)
-constexpr int W_TILE = 128 * 128;        // 16 KB of weights per 128-row block and K-block
+constexpr int NTOK = 16;                 // activation rows per tile (MMA N)
+constexpr int W_TILE = 128 * 128;        // 16 KB: 128 weight rows x one 128-wide K-block
 constexpr int A_TILE = NTOK * 128;       // 2 KB
+constexpr int STAGE_BYTES = 2 * W_TILE + A_TILE;
+constexpr int STAGES = 6;
+constexpr int COLS = 2 * NTOK;           // TMEM columns per K-block
+constexpr int NBUF = 512 / COLS;         // TMEM ring depth in K-blocks
 constexpr int THREADS = 256;             // producer, MMA, 4 promotion warps, 2 spare (scan width)
 constexpr int EPI_WARPS = 4;
+constexpr int NT1 = kInter / 128;        // 16 GEMM1 tiles per expert and token tile
+constexpr int NT2 = kHidden / 256;       // 28 GEMM2 tiles per expert and term tile
+constexpr int KB1 = kHiddenBlocks;       // 56
+constexpr int KB2 = kInterBlocks;        // 16
+constexpr int kTileEnd = -1;
 
-template <int MODE>
-struct Cfg;
-template <>
-struct Cfg<1> {
-  static constexpr int KB = kHiddenBlocks;        // 56
-  static constexpr int NT = kInter / 128;         // 16 tiles of 128 intermediate columns
-  static constexpr int W_BLOCKS = 2;              // gate + up
-  static constexpr int STAGES = 6;
-  static constexpr int ROWS_PER_PAIR = 1;
-};
-template <>
-struct Cfg<2> {
-  static constexpr int KB = kInterBlocks;         // 16
-  static constexpr int NT = kHidden / 128;        // 56 tiles of 128 output columns
-  static constexpr int W_BLOCKS = 1;
-  static constexpr int STAGES = 10;
-  static constexpr int ROWS_PER_PAIR = 2;
-};
-
-template <int MODE>
 struct Smem {
-  static constexpr int STAGE_BYTES = Cfg<MODE>::W_BLOCKS * W_TILE + A_TILE;
-  static constexpr int COLS_PER_KB = Cfg<MODE>::W_BLOCKS * NTOK;
-  static constexpr int NBUF = 512 / COLS_PER_KB;  // TMEM ring depth in K-blocks
-  uint64_t full[Cfg<MODE>::STAGES];
-  uint64_t empty[Cfg<MODE>::STAGES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
   uint64_t tfull[NBUF];
   uint64_t tempty[NBUF];
   uint64_t epi_bar[2];
-  uint64_t tab_full[2];                    // per-tile scale / token tables, filled by the producer
+  uint64_t tab_full[2];                  // per-tile table, filled by the producer
   uint64_t tab_empty[2];
   uint32_t tmem_base;
   int abort_flag;
-  int total_tiles;
   int warp_sums[8];
-  int tile_start[kMaxLocalExperts + 1];
-  int tt_cnt[kMaxLocalExperts];
+  int tiles1, tiles2;                    // GEMM1 / GEMM2 tile counts of this launch
+  int start1[kMaxLocalExperts + 1];      // GEMM1 tile prefix per expert
+  int start2[kMaxLocalExperts + 1];
+  int tt1[kMaxLocalExperts];             // token tiles per expert (GEMM1) / term tiles (GEMM2)
+  int tt2[kMaxLocalExperts];
   int row_off[kMaxLocalExperts];
   int cnt[kMaxLocalExperts];
-  alignas(16) float sa[2][Cfg<MODE>::KB][NTOK];    // activation scales of the tile's rows (per table slot)
-  alignas(16) float sw[2][2][Cfg<MODE>::KB];       // weight block scales: [gate, up][kb] or [w2][kb]
-  alignas(16) int tok[2][NTOK / 2];                // GEMM2: token and routing weight of the tile's pairs
+  int tile_id[2];                        // tile of each table slot (kTileEnd = no more work)
+  alignas(16) float sa[2][KB1][NTOK];    // activation scales of the tile's rows
+  alignas(16) float sw[2][2][KB1];       // weight block scales of the tile's two 128-row blocks
+  alignas(16) int tok[2][NTOK / 2];      // GEMM2: token and routing weight of the tile's pairs
   alignas(16) float wgt[2][NTOK / 2];
   float amax[2][EPI_WARPS][NTOK];
 };
+constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(Smem);
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
-template <int MODE>
-constexpr size_t smem_bytes() {
-  return 1024 + (size_t)Cfg<MODE>::STAGES * Smem<MODE>::STAGE_BYTES + sizeof(Smem<MODE>);
-}
+struct Tile {
+  int phase;   // 1 or 2
+  int e, nt, tt;
+};
 
 __device__ __forceinline__ int scan256(int v, int* warp_sums, int& total) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   int inc = v;
-  if (tid < 256) {
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, inc, d);
-      if (lane >= d) inc += n;
-    }
-    if (lane == 31) warp_sums[w] = inc;
+  for (int d = 1; d < 32; d <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += n;
   }
+  if (lane == 31) warp_sums[w] = inc;
   __syncthreads();
   int pre = 0, tot = 0;
 #pragma unroll
@@ -108,33 +100,47 @@ __device__ __forceinline__ int scan256(int v, int* warp_sums, int& total) {
   return pre + inc - v;
 }
 
-template <int MODE>
-__device__ __forceinline__ void decode(const Smem<MODE>& S, int E, int t, int& e, int& nt, int& tt) {
+__device__ __forceinline__ int find_expert(const int* start, int E, int t) {
   int lo = 0, hi = E - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (S.tile_start[mid] <= t) lo = mid;
+    if (start[mid] <= t) lo = mid;
     else hi = mid - 1;
   }
-  e = lo;
-  const int local = t - S.tile_start[e];
-  nt = local / S.tt_cnt[e];
-  tt = local - nt * S.tt_cnt[e];
+  return lo;
 }
 
-template <int MODE>
-__device__ __forceinline__ void set_abort(Smem<MODE>& S, int* err, int code) {
+// Queue index -> tile. Launch mode 1: GEMM1 only; 2: GEMM2 only; 3: both, GEMM1 first.
+__device__ __forceinline__ Tile decode_tile(const Smem& S, int E, int mode, int t) {
+  Tile x;
+  if (mode == 2) t += S.tiles1;
+  if (t < S.tiles1) {
+    x.phase = 1;
+    x.e = find_expert(S.start1, E, t);
+    const int local = t - S.start1[x.e];
+    x.nt = local / S.tt1[x.e];
+    x.tt = local - x.nt * S.tt1[x.e];
+  } else {
+    t -= S.tiles1;
+    x.phase = 2;
+    x.e = find_expert(S.start2, E, t);
+    const int local = t - S.start2[x.e];
+    x.nt = local / S.tt2[x.e];
+    x.tt = local - x.nt * S.tt2[x.e];
+  }
+  return x;
+}
+
+__device__ __forceinline__ void set_abort(Smem& S, int* err, int code) {
   atomicOr(err, code);
   *reinterpret_cast<volatile int*>(&S.abort_flag) = 1;
 }
-template <int MODE>
-__device__ __forceinline__ bool aborted(const Smem<MODE>& S) {
+__device__ __forceinline__ bool aborted(const Smem& S) {
   return *reinterpret_cast<const volatile int*>(&S.abort_flag) != 0;
 }
 
 // Bounded rendezvous of the four promotion warps (one mbarrier phase per use).
-template <int MODE>
-__device__ __forceinline__ bool epi_sync(Smem<MODE>& S, int& uses, int lane) {
+__device__ __forceinline__ bool epi_sync(Smem& S, int& uses, int lane) {
   const int b = uses & 1, phase = (uses >> 1) & 1;
   ++uses;
   __syncwarp();
@@ -142,19 +148,36 @@ __device__ __forceinline__ bool epi_sync(Smem<MODE>& S, int& uses, int lane) {
   return mbar_wait(smem_u32(&S.epi_bar[b]), phase);
 }
 
-template <int MODE>
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Waits (bounded) until *p >= target with acquire semantics.
+__device__ __forceinline__ bool wait_counter(const int* p, int target) {
+  if (ld_acquire(p) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire(p) < target) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
-    swap_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                     GemmArgs args) {
-  using C = Cfg<MODE>;
-  using SM = Smem<MODE>;
-  constexpr int KB = C::KB, NT = C::NT, STAGES = C::STAGES, NBUF = SM::NBUF;
-  constexpr int STAGE_BYTES = SM::STAGE_BYTES, COLS = SM::COLS_PER_KB;
+    stream_gemm_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmW13,
+                       const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmW2,
+                       DecodeArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  SM& S = *reinterpret_cast<SM*>(smem + STAGES * STAGE_BYTES);
+  Smem& S = *reinterpret_cast<Smem*>(smem + STAGES * STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int E = args.E;
+  const int E = args.E, mode = args.mode;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -168,31 +191,39 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&S.epi_bar[b]), EPI_WARPS);
       mbar_init(smem_u32(&S.tab_full[b]), 1);
-      mbar_init(smem_u32(&S.tab_empty[b]), EPI_WARPS);
+      mbar_init(smem_u32(&S.tab_empty[b]), EPI_WARPS + 1);   // promotion warps + MMA thread
     }
     S.abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmA1);
+    tma_prefetch_desc(&tmW13);
+    tma_prefetch_desc(&tmA2);
+    tma_prefetch_desc(&tmW2);
   }
   {
     const int tid = threadIdx.x;
     const int c = tid < E ? args.counts[tid] : 0;
-    const int tt = (c * C::ROWS_PER_PAIR + NTOK - 1) / NTOK;
-    int tot0, tot1;
+    const int t1 = (c + NTOK - 1) / NTOK;
+    const int t2 = (2 * c + NTOK - 1) / NTOK;
+    int tot0, tot1, tot2;
     const int roff = scan256(align_up(c, 128), S.warp_sums, tot0);
-    const int tstart = scan256(tt * NT, S.warp_sums, tot1);
+    const int s1 = scan256(t1 * NT1, S.warp_sums, tot1);
+    const int s2 = scan256(t2 * NT2, S.warp_sums, tot2);
     if (tid < E) {
       S.cnt[tid] = c;
-      S.tt_cnt[tid] = tt;
+      S.tt1[tid] = t1;
+      S.tt2[tid] = t2;
       S.row_off[tid] = roff;
-      S.tile_start[tid] = tstart;
+      S.start1[tid] = s1;
+      S.start2[tid] = s2;
     }
     if (tid == 0) {
-      S.tile_start[E] = tot1;
-      S.total_tiles = tot1;
+      S.start1[E] = tot1;
+      S.start2[E] = tot2;
+      S.tiles1 = tot1;
+      S.tiles2 = tot2;
     }
   }
   if (warp == 1) {
@@ -203,40 +234,61 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = S.tmem_base;
-  const int total = S.total_tiles;
+  const int total = mode == 1 ? S.tiles1 : mode == 2 ? S.tiles2 : S.tiles1 + S.tiles2;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ producer: tile queue, tables, TMA
     if (lane == 0) {
-      int it = 0, tile_iter = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
-        int e, nt, tt;
-        decode(S, E, t, e, nt, tt);
-        const int arow = C::ROWS_PER_PAIR * S.row_off[e] + tt * NTOK;
-        {
-          // the tile's scales (and GEMM2 token ids / weights) into table slot p
-          const int p = tile_iter & 1;
-          if (!mbar_wait(smem_u32(&S.tab_empty[p]), ((tile_iter >> 1) & 1) ^ 1)) {
+      int it = 0;
+      for (int ti = 0;; ++ti) {
+        const int p = ti & 1;
+        if (!mbar_wait(smem_u32(&S.tab_empty[p]), ((ti >> 1) & 1) ^ 1)) {
+          set_abort(S, args.err, kErrTimeoutProducer);
+          break;
+        }
+        const int t = aborted(S) ? total : atomicAdd(args.queue, 1);
+        const uint32_t tb = smem_u32(&S.tab_full[p]);
+        if (t >= total) {
+          S.tile_id[p] = kTileEnd;
+          mbar_arrive(tb);
+          break;
+        }
+        const Tile x = decode_tile(S, E, mode, t);
+        if (x.phase == 2 && mode == 3) {
+          // GEMM2 reads this expert's SwiGLU rows: wait for all of its GEMM1 tiles
+          if (!wait_counter(args.done1 + x.e, EPI_WARPS * NT1 * S.tt1[x.e])) {
             set_abort(S, args.err, kErrTimeoutProducer);
+            S.tile_id[p] = kTileEnd;
+            mbar_arrive(tb);
             break;
           }
-          const uint32_t tb = smem_u32(&S.tab_full[p]);
-          constexpr uint32_t kTabBytes = KB * NTOK * 4 + C::W_BLOCKS * KB * 4 + (MODE == 2 ? NTOK * 4 : 0);
-          mbar_arrive_expect_tx(tb, kTabBytes);
-          const size_t ld_sa = (size_t)C::ROWS_PER_PAIR * args.R1;
-          for (int kb = 0; kb < KB; ++kb)
-            bulk_load(smem_u32(&S.sa[p][kb][0]), args.sa + kb * ld_sa + arow, NTOK * 4, tb);
-          if (MODE == 1) {
-            bulk_load(smem_u32(&S.sw[p][0][0]), args.sb + ((size_t)e * 32 + nt) * kHiddenBlocks, KB * 4, tb);
-            bulk_load(smem_u32(&S.sw[p][1][0]), args.sb + ((size_t)e * 32 + 16 + nt) * kHiddenBlocks, KB * 4, tb);
-          } else {
-            bulk_load(smem_u32(&S.sw[p][0][0]), args.sb + ((size_t)e * kHiddenBlocks + nt) * kInterBlocks, KB * 4, tb);
-            const int pr = S.row_off[e] + (tt * NTOK) / 2;
-            bulk_load(smem_u32(&S.tok[p][0]), args.row_token + pr, NTOK / 2 * 4, tb);
-            bulk_load(smem_u32(&S.wgt[p][0]), args.row_weight + pr, NTOK / 2 * 4, tb);
-          }
-          ++tile_iter;
+          fence_proxy_async_global();
         }
+        S.tile_id[p] = t;
+        const int KB = x.phase == 1 ? KB1 : KB2;
+        const size_t ld_sa = x.phase == 1 ? (size_t)args.R1 : 2 * (size_t)args.R1;
+        const int arow = (x.phase == 1 ? S.row_off[x.e] : 2 * S.row_off[x.e]) + x.tt * NTOK;
+        const float* sa = x.phase == 1 ? args.sa1 : args.sa2;
+        const uint32_t bytes = KB * NTOK * 4 + 2 * KB * 4 + (x.phase == 2 ? NTOK * 4 : 0);
+        mbar_arrive_expect_tx(tb, bytes);
+        for (int kb = 0; kb < KB; ++kb)
+          bulk_load(smem_u32(&S.sa[p][kb][0]), sa + kb * ld_sa + arow, NTOK * 4, tb);
+        if (x.phase == 1) {
+          bulk_load(smem_u32(&S.sw[p][0][0]), args.s13 + ((size_t)x.e * 32 + x.nt) * KB1, KB1 * 4, tb);
+          bulk_load(smem_u32(&S.sw[p][1][0]), args.s13 + ((size_t)x.e * 32 + 16 + x.nt) * KB1, KB1 * 4, tb);
+        } else {
+          bulk_load(smem_u32(&S.sw[p][0][0]), args.s2 + ((size_t)x.e * kHiddenBlocks + 2 * x.nt) * KB2, KB2 * 4, tb);
+          bulk_load(smem_u32(&S.sw[p][1][0]), args.s2 + ((size_t)x.e * kHiddenBlocks + 2 * x.nt + 1) * KB2, KB2 * 4,
+                    tb);
+          const int pr = S.row_off[x.e] + x.tt * (NTOK / 2);
+          bulk_load(smem_u32(&S.tok[p][0]), args.row_token + pr, NTOK / 2 * 4, tb);
+          bulk_load(smem_u32(&S.wgt[p][0]), args.row_weight + pr, NTOK / 2 * 4, tb);
+        }
+        const CUtensorMap* tw = x.phase == 1 ? &tmW13 : &tmW2;
+        const CUtensorMap* ta = x.phase == 1 ? &tmA1 : &tmA2;
+        const int w0 = x.phase == 1 ? x.e * kGemm1N + x.nt * 128 : x.e * kHidden + x.nt * 256;
+        const int w1 = x.phase == 1 ? x.e * kGemm1N + kInter + x.nt * 128 : w0 + 128;
+        bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES, u = it / STAGES;
           if (!mbar_wait(smem_u32(&S.empty[s]), (u & 1) ^ 1)) {
@@ -247,22 +299,29 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t fb = smem_u32(&S.full[s]);
           const uint32_t st = smem_u32(smem + s * STAGE_BYTES);
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
-          if (MODE == 1) {
-            tma_load_2d(st, &tmW, fb, kb * 128, e * kGemm1N + nt * 128);
-            tma_load_2d(st + W_TILE, &tmW, fb, kb * 128, e * kGemm1N + kInter + nt * 128);
-          } else {
-            tma_load_2d(st, &tmW, fb, kb * 128, e * kHidden + nt * 128);
-          }
-          tma_load_2d(st + C::W_BLOCKS * W_TILE, &tmA, fb, kb * 128, arow);
+          tma_load_2d(st, tw, fb, kb * 128, w0);
+          tma_load_2d(st + W_TILE, tw, fb, kb * 128, w1);
+          tma_load_2d(st + 2 * W_TILE, ta, fb, kb * 128, arow);
         }
+        if (!ok) break;
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(128, NTOK);
       int it = 0, kt = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
+      for (int ti = 0;; ++ti) {
+        const int p = ti & 1;
+        if (!mbar_wait(smem_u32(&S.tab_full[p]), (ti >> 1) & 1)) {
+          set_abort(S, args.err, kErrTimeoutMma);
+          break;
+        }
+        const int t = S.tile_id[p];
+        mbar_arrive(smem_u32(&S.tab_empty[p]));
+        if (t == kTileEnd) break;
+        const int KB = decode_tile(S, E, mode, t).phase == 1 ? KB1 : KB2;
+        bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++it, ++kt) {
           const int s = it % STAGES, u = it / STAGES;
           const int b = kt % NBUF, v = kt / NBUF;
@@ -273,37 +332,37 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t at = st + C::W_BLOCKS * W_TILE;
+          const uint32_t at = st + 2 * W_TILE;
           const uint32_t d = tmem_base + (uint32_t)(b * COLS);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            mma_e4m3(d, sdesc_sw128(st + kk * 32), sdesc_sw128(at + kk * 32), idesc, kk > 0 ? 1u : 0u);
-            if (MODE == 1)
-              mma_e4m3(d + NTOK, sdesc_sw128(st + W_TILE + kk * 32), sdesc_sw128(at + kk * 32), idesc,
-                       kk > 0 ? 1u : 0u);
+            const uint64_t ad = sdesc_sw128(at + kk * 32);
+            mma_e4m3(d, sdesc_sw128(st + kk * 32), ad, idesc, kk > 0 ? 1u : 0u);
+            mma_e4m3(d + NTOK, sdesc_sw128(st + W_TILE + kk * 32), ad, idesc, kk > 0 ? 1u : 0u);
           }
           mma_commit(smem_u32(&S.empty[s]));
           mma_commit(smem_u32(&S.tfull[b]));
         }
+        if (!ok) break;
       }
     }
   } else if (warp < 2 + EPI_WARPS) {
     // ------------------------------------------------------------ promotion + epilogue
     const int q = warp & 3;
-    const int r = 32 * q + lane;                          // weight row inside the 128-row block
-    const int et = threadIdx.x - 64;                      // 0..127 among promotion threads
+    const int r = 32 * q + lane;                          // weight row inside each 128-row block
     const uint32_t lane_addr = tmem_base + ((uint32_t)(32 * q) << 16);
-    int kt = 0, tile_iter = 0, sync_uses = 0;
-    for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++tile_iter) {
-      int e, nt, tt;
-      decode(S, E, t, e, nt, tt);
-      const int p = tile_iter & 1;
-      const int row0 = C::ROWS_PER_PAIR * S.row_off[e] + tt * NTOK;     // first GEMM row of the tile
-      const int nvalid = min(NTOK, C::ROWS_PER_PAIR * S.cnt[e] - tt * NTOK);
-      if (!mbar_wait(smem_u32(&S.tab_full[p]), (tile_iter >> 1) & 1)) {
+    int kt = 0, sync_uses = 0;
+    for (int ti = 0;; ++ti) {
+      const int p = ti & 1;
+      if (!mbar_wait(smem_u32(&S.tab_full[p]), (ti >> 1) & 1)) {
         set_abort(S, args.err, kErrTimeoutEpilogue);
         break;
       }
+      const int t = S.tile_id[p];
+      if (t == kTileEnd) break;
+      const Tile x = decode_tile(S, E, mode, t);
+      const int KB = x.phase == 1 ? KB1 : KB2;
+      const int nvalid = min(NTOK, (x.phase == 1 ? S.cnt[x.e] : 2 * S.cnt[x.e]) - x.tt * NTOK);
       float g[NTOK], u[NTOK];
 #pragma unroll
       for (int i = 0; i < NTOK; ++i) g[i] = u[i] = 0.f;
@@ -316,25 +375,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        float pg[NTOK], pu[NTOK];
-        tmem_ld16(lane_addr + (uint32_t)(b * COLS), pg);
-        if (MODE == 1) tmem_ld16(lane_addr + (uint32_t)(b * COLS + NTOK), pu);
+        float p0[NTOK], p1[NTOK];
+        tmem_ld16(lane_addr + (uint32_t)(b * COLS), p0);
+        tmem_ld16(lane_addr + (uint32_t)(b * COLS + NTOK), p1);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&S.tempty[b]));
-        const float swg = S.sw[p][0][kb];
-        const float swu = MODE == 1 ? S.sw[p][1][kb] : 0.f;
+        const float sw0 = S.sw[p][0][kb], sw1 = S.sw[p][1][kb];
 #pragma unroll
         for (int i = 0; i < NTOK; ++i) {
           const float sa = S.sa[p][kb][i];
-          g[i] = fmaf(pg[i], sa * swg, g[i]);
-          if (MODE == 1) u[i] = fmaf(pu[i], sa * swu, u[i]);
+          g[i] = fmaf(p0[i], sa * sw0, g[i]);
+          u[i] = fmaf(p1[i], sa * sw1, u[i]);
         }
       }
       if (!ok) break;
 
-      if (MODE == 1) {
+      if (x.phase == 1) {
         // C = silu(X2) * X1 for this thread's intermediate column and the tile's tokens
         float am[NTOK];
 #pragma unroll
@@ -358,34 +416,47 @@ __global__ void __launch_bounds__(THREADS, 1)
           set_abort(S, args.err, kErrTimeoutEpilogue);
           break;
         }
-        const int col = nt * 128 + r;
+        const int col = x.nt * 128 + r;
+        const size_t prow0 = (size_t)S.row_off[x.e] + x.tt * NTOK;
 #pragma unroll
         for (int i = 0; i < NTOK; ++i) {
-          if (i >= nvalid) break;
-          const float amax = fmaxf(fmaxf(S.amax[p][0][i], S.amax[p][1][i]), fmaxf(S.amax[p][2][i], S.amax[p][3][i]));
-          const float s_hi = amax / kFp8Max;
-          const float inv_hi = amax > 0.f ? kFp8Max / amax : 0.f;
-          const __nv_fp8_storage_t hq = __nv_cvt_float_to_fp8(g[i] * inv_hi, __NV_SATFINITE, __NV_E4M3);
-          const __half_raw hh = __nv_cvt_fp8_to_halfraw(hq, __NV_E4M3);
-          const float hv = __half2float(*reinterpret_cast<const __half*>(&hh));
-          const __nv_fp8_storage_t lq =
-              __nv_cvt_float_to_fp8((g[i] - hv * s_hi) * (inv_hi * 16.0f), __NV_SATFINITE, __NV_E4M3);
-          const size_t prow = (size_t)row0 + i;           // pair row (GEMM1 rows are pair rows)
-          args.a2[(2 * prow) * kInter + col] = hq;
-          args.a2[(2 * prow + 1) * kInter + col] = lq;
-          if (r == 0) {
-            float* sa2 = args.sa2 + (size_t)nt * 2 * args.R1 + 2 * prow;
-            sa2[0] = s_hi;
-            sa2[1] = s_hi * (1.0f / 16.0f);
+          if (i < nvalid) {
+            const float amax =
+                fmaxf(fmaxf(S.amax[p][0][i], S.amax[p][1][i]), fmaxf(S.amax[p][2][i], S.amax[p][3][i]));
+            const float s_hi = amax / kFp8Max;
+            const float inv_hi = amax > 0.f ? kFp8Max / amax : 0.f;
+            const __nv_fp8_storage_t hq = __nv_cvt_float_to_fp8(g[i] * inv_hi, __NV_SATFINITE, __NV_E4M3);
+            const __half_raw hh = __nv_cvt_fp8_to_halfraw(hq, __NV_E4M3);
+            const float hv = __half2float(*reinterpret_cast<const __half*>(&hh));
+            const __nv_fp8_storage_t lq =
+                __nv_cvt_float_to_fp8((g[i] - hv * s_hi) * (inv_hi * 16.0f), __NV_SATFINITE, __NV_E4M3);
+            const size_t prow = prow0 + i;
+            args.a2[(2 * prow) * kInter + col] = hq;
+            args.a2[(2 * prow + 1) * kInter + col] = lq;
+            if (r == 0) {
+              float* sa2 = args.sa2 + (size_t)x.nt * 2 * args.R1 + 2 * prow;
+              sa2[0] = s_hi;
+              sa2[1] = s_hi * (1.0f / 16.0f);
+            }
           }
         }
+        if (mode == 3) {
+          // publish: this warp's part of the expert's SwiGLU rows is written
+          fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(args.done1 + x.e, 1);
+        }
       } else {
-        const int col = nt * 128 + r;
+        const int col = x.nt * 256 + r;
 #pragma unroll
         for (int i = 0; i < NTOK / 2; ++i) {
-          if (2 * i >= nvalid) break;
-          const float v = (g[2 * i] + g[2 * i + 1]) * S.wgt[p][i];
-          atomicAdd(args.out_acc + (size_t)S.tok[p][i] * kHidden + col, v);
+          if (2 * i < nvalid) {
+            const float w = S.wgt[p][i];
+            float* dst = args.out_acc + (size_t)S.tok[p][i] * kHidden + col;
+            atomicAdd(dst, (g[2 * i] + g[2 * i + 1]) * w);
+            atomicAdd(dst + 128, (u[2 * i] + u[2 * i + 1]) * w);
+          }
         }
       }
       __syncwarp();
@@ -399,36 +470,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
-}
-
-static int g_attr_set[2][64];
-
-template <int MODE>
-cudaError_t launch(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& args, int num_sms,
-                   cudaStream_t st) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  constexpr size_t bytes = smem_bytes<MODE>();
-  static_assert(bytes <= 232448, "shared memory budget");
-  if (dev >= 64 || !g_attr_set[MODE - 1][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(swap_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)bytes);
-    if (e != cudaSuccess) return e;
-    if (dev < 64) g_attr_set[MODE - 1][dev] = 1;
+  // the last CTA to leave re-arms the queue, so a launch can be repeated
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(args.queue + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(args.queue, 0);
+      atomicExch(args.queue + 1, 0);
+      if (mode == 3)
+        for (int e = 0; e < E; ++e) atomicExch(args.done1 + e, 0);
+    }
   }
-  swap_gemm_kernel<MODE><<<num_sms, THREADS, bytes, st>>>(tmA, tmW, args);
-  return cudaGetLastError();
 }
+
+static int g_attr_set[64];
 
 }  // namespace dec
 
-cudaError_t launch_gemm1_decode(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& args,
-                                int num_sms, cudaStream_t st) {
-  return dec::launch<1>(tmA, tmW, args, num_sms, st);
-}
-cudaError_t launch_gemm2_decode(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& args,
-                                int num_sms, cudaStream_t st) {
-  return dec::launch<2>(tmA, tmW, args, num_sms, st);
+cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13, const CUtensorMap& tmA2,
+                               const CUtensorMap& tmW2, const DecodeArgs& args, int num_sms, cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !dec::g_attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(dec::stream_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)dec::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) dec::g_attr_set[dev] = 1;
+  }
+  dec::stream_gemm_kernel<<<num_sms, dec::THREADS, dec::SMEM_BYTES, st>>>(tmA1, tmW13, tmA2, tmW2, args);
+  return cudaGetLastError();
 }
 
 }  // namespace moe

@@ -73,6 +73,8 @@ int num_sms_of_current_device() {
   return n;
 }
 
+int gemm_path(int T);
+
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 int check_workspace(void* ws, size_t bytes, int T, int E) {
@@ -96,7 +98,10 @@ size_t moe_fp8_workspace_bytes(int32_t max_tokens, int32_t num_local_experts) {
   return moe::ws_layout(max_tokens, num_local_experts).total;
 }
 
-int32_t moe_fp8_kernels_per_call(int32_t num_tokens) { return num_tokens > 0 ? 5 : 0; }
+int32_t moe_fp8_kernels_per_call(int32_t num_tokens) {
+  if (num_tokens <= 0) return 0;
+  return gemm_path(num_tokens) == 2 ? 4 : 5;
+}
 
 int moe_fp8_workspace_view(void* workspace, int32_t T, int32_t E, MoeFp8WorkspaceView* view) {
   if (!workspace || !view || T < 0 || E < 1 || E > moe::kMaxLocalExperts)
@@ -157,21 +162,26 @@ struct Plan {
   int* counts; int* topk_idx; float* topk_w; int* pair_pos; int* row_token; float* row_weight;
   uint8_t* a1; float* sa1; uint8_t* a2; float* sa2; float* acc; int* err;
   CUtensorMap tmA1, tmB1, tmA2, tmB2;
-  bool decode1, decode2;  // weight-streaming (swap-AB) GEMM1 / GEMM2 kernels
+  int path;  // see gemm_path()
 };
 
-// Calls with at most this many tokens use the decode-shaped GEMM kernels
-// (few tokens per expert; weights on the MMA's M side). Measured crossovers on B200: the weight-streaming GEMM1 wins up to a few
-// hundred tokens, the weight-streaming GEMM2 only up to about a hundred.
-std::atomic<int> g_decode_max_tokens[2] = {{-1}, {-1}};
-int decode_max_tokens(int which) {
-  int v = g_decode_max_tokens[which].load(std::memory_order_relaxed);
-  if (v < 0) {
-    const char* e = getenv("MOE_DECODE_MAX_TOKENS");
-    v = e ? atoi(e) : (which == 0 ? 256 : 96);
-    g_decode_max_tokens[which].store(v, std::memory_order_relaxed);
+// GEMM kernel families per call:
+//   0  128-row tile kernels for both GEMMs
+//   1  weight-streaming GEMM1, tile GEMM2
+//   2  one weight-streaming launch for GEMM1 and GEMM2 (fused queue)
+//   3  weight-streaming GEMM1 and GEMM2 as two launches
+// Automatic choice from measured crossovers on B200 (offset-0 routing, 32
+// local experts): the fused streaming launch up to 384 tokens, tile kernels above.
+std::atomic<int> g_forced_path{-2};
+int gemm_path(int T) {
+  int f = g_forced_path.load(std::memory_order_relaxed);
+  if (f == -2) {
+    const char* e = getenv("MOE_GEMM_PATH");
+    f = e ? atoi(e) : -1;
+    g_forced_path.store(f, std::memory_order_relaxed);
   }
-  return v;
+  if (f >= 0 && f <= 3) return f;
+  return T <= 384 ? 2 : 0;
 }
 
 int make_plan(const MoeFp8Args* a, Plan& p) {
@@ -207,12 +217,12 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
   p.sa2 = reinterpret_cast<float*>(w + L.sa2);
   p.acc = reinterpret_cast<float*>(w + L.out_acc);
   p.err = reinterpret_cast<int*>(w + L.err);
-  p.decode1 = T <= decode_max_tokens(0);
-  p.decode2 = T <= decode_max_tokens(1);
-  const uint32_t w2_box = p.decode2 ? 128 : 256;
-  if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, p.decode1 ? 16 : 128) ||
+  p.path = gemm_path(T);
+  const bool s1 = p.path != 0, s2 = p.path >= 2;
+  const uint32_t w2_box = s2 ? 128 : 256;
+  if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, s1 ? 16 : 128) ||
       !encode_fp8_2d(&p.tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128) ||
-      !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, p.decode2 ? 16 : 128) ||
+      !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, s2 ? 16 : 128) ||
       !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, w2_box))
     return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   return MOE_OK;
@@ -224,7 +234,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
   cudaError_t e = cudaSuccess;
   switch (stage) {
     case 0:
-      e = cudaMemsetAsync(p.counts, 0, sizeof(int32_t) * E, st);
+      e = cudaMemsetAsync(p.counts, 0, moe::WsLayout::kCountersBytes, st);
       if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
       e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
                             a->local_expert_offset, E, a->routed_scaling_factor, p.topk_idx, p.topk_w, p.pair_pos,
@@ -237,35 +247,71 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
                               p.sa1, p.row_token, p.row_weight, p.nsm, st);
       if (e != cudaSuccess) return cuda_fail(e, "permute kernel launch");
       break;
-    case 2: {
-      moe::GemmArgs g{};
-      g.counts = p.counts;
-      g.E = E;
-      g.R1 = p.L.R1;
-      g.sa = p.sa1;
-      g.sb = a->gemm1_weights_scale;
-      g.a2 = p.a2;
-      g.sa2 = p.sa2;
-      g.err = p.err;
-      e = p.decode1 ? moe::launch_gemm1_decode(p.tmA1, p.tmB1, g, p.nsm, st)
-                   : moe::launch_gemm1(p.tmA1, p.tmB1, g, p.nsm, st);
-      if (e != cudaSuccess) return cuda_fail(e, "GEMM1 launch");
-      break;
-    }
+    case 2:
     case 3: {
+      if (p.path >= 2) {
+        // streaming kernel: path 2 does both GEMMs in stage 2; path 3 one GEMM per stage
+        if (p.path == 2 && stage == 3) break;
+        uint8_t* w = static_cast<uint8_t*>(a->workspace);
+        moe::DecodeArgs d{};
+        d.mode = p.path == 2 ? 3 : stage - 1;
+        d.E = E;
+        d.R1 = p.L.R1;
+        d.counts = p.counts;
+        d.sa1 = p.sa1;
+        d.sa2 = p.sa2;
+        d.s13 = a->gemm1_weights_scale;
+        d.s2 = a->gemm2_weights_scale;
+        d.a2 = p.a2;
+        d.row_token = p.row_token;
+        d.row_weight = p.row_weight;
+        d.out_acc = p.acc;
+        d.err = p.err;
+        d.queue = reinterpret_cast<int*>(w + p.L.queue());
+        d.done1 = reinterpret_cast<int*>(w + p.L.done1());
+        e = moe::launch_stream_gemm(p.tmA1, p.tmB1, p.tmA2, p.tmB2, d, p.nsm, st);
+        if (e != cudaSuccess) return cuda_fail(e, "streaming GEMM launch");
+        break;
+      }
+      if (stage == 2 && p.path == 1) {
+        moe::DecodeArgs d{};
+        uint8_t* w = static_cast<uint8_t*>(a->workspace);
+        d.mode = 1;
+        d.E = E;
+        d.R1 = p.L.R1;
+        d.counts = p.counts;
+        d.sa1 = p.sa1;
+        d.sa2 = p.sa2;
+        d.s13 = a->gemm1_weights_scale;
+        d.s2 = a->gemm2_weights_scale;
+        d.a2 = p.a2;
+        d.err = p.err;
+        d.queue = reinterpret_cast<int*>(w + p.L.queue());
+        d.done1 = reinterpret_cast<int*>(w + p.L.done1());
+        e = moe::launch_stream_gemm(p.tmA1, p.tmB1, p.tmA2, p.tmB2, d, p.nsm, st);
+        if (e != cudaSuccess) return cuda_fail(e, "streaming GEMM1 launch");
+        break;
+      }
       moe::GemmArgs g{};
       g.counts = p.counts;
       g.E = E;
       g.R1 = p.L.R1;
-      g.sa = p.sa2;
-      g.sb = a->gemm2_weights_scale;
-      g.row_token = p.row_token;
-      g.row_weight = p.row_weight;
-      g.out_acc = p.acc;
       g.err = p.err;
-      e = p.decode2 ? moe::launch_gemm2_decode(p.tmA2, p.tmB2, g, p.nsm, st)
-                   : moe::launch_gemm2(p.tmA2, p.tmB2, g, p.nsm, st);
-      if (e != cudaSuccess) return cuda_fail(e, "GEMM2 launch");
+      if (stage == 2) {
+        g.sa = p.sa1;
+        g.sb = a->gemm1_weights_scale;
+        g.a2 = p.a2;
+        g.sa2 = p.sa2;
+        e = moe::launch_gemm1(p.tmA1, p.tmB1, g, p.nsm, st);
+      } else {
+        g.sa = p.sa2;
+        g.sb = a->gemm2_weights_scale;
+        g.row_token = p.row_token;
+        g.row_weight = p.row_weight;
+        g.out_acc = p.acc;
+        e = moe::launch_gemm2(p.tmA2, p.tmB2, g, p.nsm, st);
+      }
+      if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
       break;
     }
     case 4:
@@ -292,14 +338,14 @@ int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
   return MOE_OK;
 }
 
-int32_t moe_fp8_set_decode_max_tokens(int32_t max_tokens) {
-  const int32_t old = decode_max_tokens(0);
-  if (max_tokens >= 0) {
-    g_decode_max_tokens[0].store(max_tokens, std::memory_order_relaxed);
-    g_decode_max_tokens[1].store(max_tokens, std::memory_order_relaxed);
-  }
+int32_t moe_fp8_set_gemm_path(int32_t path) {
+  gemm_path(0);  // resolve the environment default once
+  const int32_t old = g_forced_path.load(std::memory_order_relaxed);
+  if (path >= -1 && path <= 3) g_forced_path.store(path, std::memory_order_relaxed);
   return old;
 }
+
+int32_t moe_fp8_gemm_path(int32_t num_tokens) { return gemm_path(num_tokens); }
 
 // Profiling aid: timeline of the GEMM kernels' CTA 0 (see grouped_gemm.cu).
 int moe_fp8_debug_trace(int32_t enable, uint64_t* host, int32_t n) {

@@ -28,10 +28,25 @@ cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E,
                            const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
                            float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st);
 cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, int num_sms, cudaStream_t st);
-cudaError_t launch_gemm1_decode(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& args,
-                                int num_sms, cudaStream_t st);
-cudaError_t launch_gemm2_decode(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& args,
-                                int num_sms, cudaStream_t st);
+// Weight-streaming GEMM kernel (decode_gemm.cu).
+struct DecodeArgs {
+  int mode;                // 1: GEMM1 tiles, 2: GEMM2 tiles, 3: both in one launch
+  int E, R1;
+  const int* counts;
+  const float* sa1;        // [56, R1]
+  float* sa2;              // [16, 2*R1] (written by GEMM1 tiles)
+  const float* s13;        // [E, 32, 56]
+  const float* s2;         // [E, 56, 16]
+  uint8_t* a2;             // e4m3 [2*R1, 2048]
+  const int* row_token;
+  const float* row_weight;
+  float* out_acc;
+  int* err;
+  int* queue;              // [2]: tile counter, CTA exit counter (zero before the first launch)
+  int* done1;              // [E]: finished GEMM1 tile parts per expert (mode 3)
+};
+cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13, const CUtensorMap& tmA2,
+                               const CUtensorMap& tmW2, const DecodeArgs& args, int num_sms, cudaStream_t st);
 cudaError_t set_trace(int on);
 cudaError_t read_trace(unsigned long long* host, int n);
 cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,

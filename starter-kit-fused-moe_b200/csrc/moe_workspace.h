@@ -15,7 +15,8 @@ namespace moe {
 struct WsLayout {
   int T, E, R1;               // tokens, local experts, pair-row capacity
   size_t err;                 // int32 error word (sticky; cleared by the host reader)
-  size_t counts;              // int32 [E]   pairs per local expert
+  size_t counts;              // int32 [E]   pairs per local expert, then the streaming kernel's
+                              //             tile queue [2] and per-expert GEMM1 progress [256]
   size_t topk_idx;            // int32 [T*8] selected global experts (selection order)
   size_t topk_w;              // f32   [T*8] combine weights
   size_t pair_pos;            // int32 [T*8] position inside the expert's group, -1 if not local
@@ -27,6 +28,9 @@ struct WsLayout {
   size_t sa2;                 // f32   [16, 2*R1]   their 1x128 scales
   size_t out_acc;             // f32   [T, 7168]    combine accumulator
   size_t total;
+  size_t queue() const { return counts + sizeof(int32_t) * 256; }
+  size_t done1() const { return counts + sizeof(int32_t) * 258; }
+  static constexpr size_t kCountersBytes = sizeof(int32_t) * (256 + 2 + 256);
 };
 
 inline size_t ws_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -42,7 +46,7 @@ inline WsLayout ws_layout(int T, int E) {
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t r = o; o = ws_align(o + bytes, 1024); return r; };
   L.err = take(256);
-  L.counts = take(sizeof(int32_t) * 256);
+  L.counts = take(sizeof(int32_t) * (256 + 2 + 256));
   L.topk_idx = take(sizeof(int32_t) * 8 * (size_t)T);
   L.topk_w = take(sizeof(float) * 8 * (size_t)T);
   L.pair_pos = take(sizeof(int32_t) * 8 * (size_t)T);

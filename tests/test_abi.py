@@ -39,7 +39,10 @@ def test_workspace_size_monotonic(pkg):
 
 def test_kernels_per_call(pkg):
     lib = pkg.load_library()
-    assert lib.moe_fp8_kernels_per_call(0) == 0 and lib.moe_fp8_kernels_per_call(16) == 5
+    assert lib.moe_fp8_kernels_per_call(0) == 0
+    assert lib.moe_fp8_kernels_per_call(16) == 4        # routing, permute, fused streaming GEMMs, finalize
+    assert lib.moe_fp8_kernels_per_call(4096) == 5
+    assert [lib.moe_fp8_gemm_path(t) for t in (1, 96, 384, 385, 4096)] == [2, 2, 2, 0, 0]
 
 
 def test_invalid_arguments_rejected_before_any_launch(pkg):

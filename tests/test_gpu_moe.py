@@ -76,12 +76,12 @@ def gpu_inputs(pkg):
     torch.cuda.empty_cache()
 
 
-@pytest.fixture(params=["decode", "tiles"])
+@pytest.fixture(params=[0, 1, 2, 3])
 def kernel_path(request, pkg):
-    """Run a test through the weight-streaming kernels or the 128-row tile kernels."""
-    old = pkg.set_decode_max_tokens(1 << 30 if request.param == "decode" else 0)
+    """Run a test through each GEMM kernel family (tile / streaming / fused streaming)."""
+    old = pkg.set_gemm_path(request.param)
     yield request.param
-    pkg.set_decode_max_tokens(old)
+    pkg.set_gemm_path(old)
 
 
 @pytest.mark.parametrize("T", [2, 17, 64, 200])
@@ -104,14 +104,36 @@ def test_many_tokens_per_expert(kernel_path, pkg, oracle, gpu_inputs):
     print(f"skewed T=600 {kernel_path}: max_abs_err={err:.3e}")
 
 
-def test_both_paths_agree(pkg, gpu_inputs):
+def test_all_paths_agree(pkg, gpu_inputs):
     x = gpu_inputs(64, seed=31)
-    old = pkg.set_decode_max_tokens(1 << 30)
-    a = pkg.run(*x.args()).float()
-    pkg.set_decode_max_tokens(0)
-    b = pkg.run(*x.args()).float()
-    pkg.set_decode_max_tokens(old)
-    assert torch.allclose(a, b, atol=4e-3, rtol=1e-2)
+    outs = []
+    for path in (0, 1, 2, 3):
+        old = pkg.set_gemm_path(path)
+        outs.append(pkg.run(*x.args()).float())
+        pkg.set_gemm_path(old)
+    torch.cuda.synchronize()
+    assert pkg.read_device_error() == 0
+    for o in outs[1:]:
+        assert torch.allclose(outs[0], o, atol=4e-3, rtol=1e-2)
+
+
+def test_fused_path_repeated_and_stage_relaunch(pkg, oracle, gpu_inputs):
+    """The streaming kernel's tile queue re-arms itself: repeated calls and stage-alone re-launches."""
+    import bench
+    x = gpu_inputs(40, seed=41)
+    old = pkg.set_gemm_path(2)
+    try:
+        op = bench.Op(pkg, x)
+        for _ in range(3):
+            op()
+        op.stage(2)            # fused GEMM1+GEMM2 again (adds a second copy into the accumulator)
+        op.stage(4)
+        torch.cuda.synchronize()
+        assert pkg.read_device_error() == 0
+        ref = oracle.moe_forward(*x.args(), out_dtype="f32") * 2
+        assert_close(op.out.float().cpu().numpy(), oracle.bf16_round(ref), what="stage relaunch")
+    finally:
+        pkg.set_gemm_path(old)
 
 
 @pytest.mark.parametrize("offset", [32, 224])
