@@ -112,6 +112,23 @@ int moe_fp8_workspace_view(void* workspace, int32_t num_tokens, int32_t num_loca
  * checks CUDA errors after its launches (solution/cuda/kernel.cu:19-23). */
 int moe_fp8_read_device_error(void* workspace, void* stream, int32_t* bits);
 
+/* Routing without a workspace, for callers that may not allocate device
+ * memory where they call this operator (a TensorRT plugin's enqueue, an XLA
+ * custom call limited to the buffers its framework planned, a serving engine
+ * that reserved its memory pool at start-up and forbids cudaMalloc afterwards).
+ * Same kernel and results as moe_fp8_route; writes topk_idx [T, 8] and
+ * topk_weights [T, 8] (device pointers). Its scratch (per-expert counters and
+ * selection positions) is a fixed array inside this library's device image:
+ * up to 16,384 tokens (larger T is rejected with MOE_ERR_INVALID_ARGUMENT),
+ * about 513 KB held on every GPU that loads the library until exit. Every call
+ * shares that array (the counters are cleared at the start of each call), so
+ * calls that overlap on the GPU race and must be serialised by the caller. The
+ * first call on a device looks up the array's address and should come before
+ * any stream capture. No counterpart in the reference. */
+int moe_fp8_route_static(const float* routing_logits, const void* routing_bias, int32_t num_tokens,
+                         int32_t local_expert_offset, int32_t num_local_experts, float routed_scaling_factor,
+                         int32_t* topk_idx, float* topk_weights, void* stream);
+
 /* Text of the last error on the calling thread (the reference raises the
  * equivalent message through TVM_FFI_ICHECK, solution/cuda/main.cpp:20-34). */
 const char* moe_fp8_last_error(void);

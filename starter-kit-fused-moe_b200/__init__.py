@@ -66,7 +66,7 @@ class MoeFp8WorkspaceView(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "moe_fp8_block_scale_run", "moe_fp8_workspace_bytes", "moe_fp8_route", "moe_fp8_workspace_view",
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
-    "moe_fp8_set_gemm_path", "moe_fp8_gemm_path",
+    "moe_fp8_set_gemm_path", "moe_fp8_gemm_path", "moe_fp8_route_static",
 )
 
 _lib = None
@@ -92,6 +92,8 @@ def load_library(path: str | pathlib.Path | None = None) -> ctypes.CDLL:
         lib.moe_fp8_workspace_bytes.restype = sz
         lib.moe_fp8_route.argtypes = [vp, vp, i32, i32, i32, ctypes.c_float, vp, sz, vp]
         lib.moe_fp8_route.restype = ctypes.c_int
+        lib.moe_fp8_route_static.argtypes = [vp, vp, i32, i32, i32, ctypes.c_float, vp, vp, vp]
+        lib.moe_fp8_route_static.restype = ctypes.c_int
         lib.moe_fp8_workspace_view.argtypes = [vp, i32, i32, ctypes.POINTER(MoeFp8WorkspaceView)]
         lib.moe_fp8_workspace_view.restype = ctypes.c_int
         lib.moe_fp8_read_device_error.argtypes = [vp, vp, ctypes.POINTER(i32)]

@@ -89,6 +89,8 @@ int check_workspace(void* ws, size_t bytes, int T, int E) {
 
 }  // namespace
 
+void moe::set_last_error(const char* msg) { g_last_error = msg; }
+
 extern "C" {
 
 const char* moe_fp8_last_error(void) { return g_last_error.c_str(); }

@@ -47,6 +47,8 @@ struct DecodeArgs {
 };
 cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13, const CUtensorMap& tmA2,
                                const CUtensorMap& tmW2, const DecodeArgs& args, int num_sms, cudaStream_t st);
+// Text returned by moe_fp8_last_error() on the calling thread.
+void set_last_error(const char* msg);
 cudaError_t set_trace(int on);
 cudaError_t read_trace(unsigned long long* host, int n);
 cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
