@@ -194,16 +194,30 @@ def cpu_reference_time(pkg, O, x, max_seconds=60.0):
 
 
 def run_reference_arm(a, world, rank):
+    """CPU reference path (the numpy oracle restating the definition's PyTorch
+    reference) on the host cores, on this arm's workload: the T-token decode call
+    at N=1; at N>1 the expert-parallel job (all ranks' tokens over 256 experts),
+    timed on a 64-token sample and scaled linearly to the job's token count."""
     if rank != 0:
         return
     pkg = ge.load_package()
     O = ge.load_oracle()
-    x = pkg.inputs.make_inputs(a.tokens, seed=0)
+    if world == 1:
+        x = pkg.inputs.make_inputs(a.tokens, seed=0)
+        scale, sample = 1.0, f"full operator call at T={a.tokens}, 32 local experts"
+        workload = f"decode T={a.tokens} tokens per GPU, E_local=32, local_expert_offset=0"
+    else:
+        n = 64
+        x = pkg.inputs.make_inputs(n, seed=100, num_local_experts=256, weight_experts=8)
+        scale = world * a.ep_tokens / n
+        sample = (f"{n} tokens over all 256 experts, scaled x{scale:.0f} to {world} ranks x {a.ep_tokens} tokens "
+                  f"(linear in tokens)")
+        workload = f"expert parallel: {a.ep_tokens} tokens per GPU, 256 experts over {world} GPUs"
     times = []
     budget = 240.0
     t_start = time.perf_counter()
     for i in range(a.warmup + a.steps):
-        dt = cpu_reference_time(pkg, O, x)
+        dt = cpu_reference_time(pkg, O, x) * scale
         if i >= a.warmup:
             times.append(dt)
         if time.perf_counter() - t_start > budget and len(times) >= 1:
@@ -214,13 +228,84 @@ def run_reference_arm(a, world, rank):
             "warmup": a.warmup, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, benchmark distributions)",
             "impl": "reference",
-            "config": {"workload": f"decode T={a.tokens}, E_local=32, offset 0", "tokens": a.tokens,
-                       "parallelism": "replicas"},
+            "config": {"workload": workload, "parallelism": "cpu"},
             "cpu_baseline": {"value": us, "unit": "us", "cores": cores, "kind": "port",
-                             "sample": f"full operator call at T={a.tokens} (numpy restatement of the "
-                                       f"definition's PyTorch reference; hit experts dequantised)"},
+                             "sample": sample + " (numpy restatement of the definition's PyTorch reference; "
+                                                "hit experts dequantised)"},
             "e2e": {"value": us, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def run_ep_bench(a, world, rank):
+    """expert parallel over `world` GPUs, 256/world experts per
+    rank, `--ep-tokens` tokens per rank, NCCL all-to-all dispatch and combine."""
+    pkg = ge.load_package()
+    import fused_moe_b200.ep as ep
+    hbm_peak, bf16_peak, peak_kind = load_peaks()
+    T = a.ep_tokens
+    epr = 256 // world
+    w = pkg.inputs.make_inputs(8, seed=0, device="cuda", num_local_experts=epr, weight_experts=8,
+                               local_expert_offset=rank * epr)
+    x = pkg.inputs.make_inputs(T, seed=100 + rank, device="cuda", weight_experts=1)
+    stats = {}
+
+    def step():
+        return ep.ep_forward(x.routing_logits, w.routing_bias, x.hidden_states, x.hidden_states_scale,
+                             w.gemm1_weights, w.gemm1_weights_scale, w.gemm2_weights, w.gemm2_weights_scale, 2.5,
+                             stats=stats)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    barrier(world)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        per = timed(step, a.steps, flush)
+    barrier(world)
+    ms = max_over_ranks(sum(per), world) / a.steps
+    # every rank's T tokens x 8 picks are computed somewhere in the job
+    flops_all = float(world) * T * 8 * FLOPS_PER_PAIR
+    # end to end: this rank's inputs from pinned host memory, output back
+    pin = lambda t: t.cpu().pin_memory()
+    h_in = [pin(t) for t in (x.routing_logits, x.hidden_states, x.hidden_states_scale)]
+    d_in = [torch.empty_like(t, device="cuda") for t in h_in]
+    h_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        for d, h in zip(d_in, h_in):
+            d.copy_(h, non_blocking=True)
+        o = ep.ep_forward(d_in[0], w.routing_bias, d_in[1], d_in[2], w.gemm1_weights, w.gemm1_weights_scale,
+                          w.gemm2_weights, w.gemm2_weights_scale, 2.5)
+        h_out.copy_(o, non_blocking=True)
+
+    e2e_step()
+    barrier(world)
+    e2e_ms = max_over_ranks(sum(timed(e2e_step, a.steps, flush)), world) / a.steps
+    fp8_peak = 2 * bf16_peak
+    tfl = flops_all / (ms * 1e-3) / 1e12
+    line = {
+        "metric": "fused_moe_us_per_call", "value": ms * 1e3, "unit": "us", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)",
+        "data": "synthetic (seeded, benchmark distributions; random-init weights)",
+        "config": {"workload": f"expert parallel: {T} tokens per GPU, 256 experts ({epr} per GPU, "
+                               f"local_expert_offset = {epr}*rank), NCCL all-to-all dispatch and combine",
+                   "tokens_per_rank": T, "experts_per_rank": epr, "parallelism": f"ep{world}",
+                   "sent_tokens_rank0": stats.get("sent_tokens"), "received_tokens_rank0": stats.get("received_tokens"),
+                   "l2": "flushed (256 MB write) between timed calls"},
+        "tflops": tfl,
+        "roofline": {"kernel": "whole expert-parallel step (dispatch + local grouped GEMMs + combine)",
+                     "bound": "tensor", "achieved": tfl, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": tfl / fp8_peak, "peak_kind": "2x measured dense bf16 (FP8 peak not measured)",
+                     "traffic": None},
+        "e2e": {"value": e2e_ms * 1e3, "unit": "us",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in h_in),
+                "d2h_bytes_per_step": h_out.numel() * h_out.element_size()},
+        "gpu_launches": a.steps * (int(pkg.load_library().moe_fp8_kernels_per_call(T)) + 6),
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, n=5, warm=3):
@@ -252,12 +337,19 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-tokens", type=int, default=8192, help="tokens per rank in the multi-GPU (EP) run")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     world, rank, local = dist_setup() if a.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
                                                                  int(os.environ.get("RANK", "0")), 0)
     if a.impl == "reference":
         run_reference_arm(a, world, rank)
+        return
+
+    if world > 1:
+        run_ep_bench(a, world, rank)
+        import torch.distributed as dist
+        dist.destroy_process_group()
         return
 
     pkg = ge.load_package()

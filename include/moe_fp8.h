@@ -129,6 +129,29 @@ int moe_fp8_route_static(const float* routing_logits, const void* routing_bias, 
                          int32_t local_expert_offset, int32_t num_local_experts, float routed_scaling_factor,
                          int32_t* topk_idx, float* topk_weights, void* stream);
 
+/* ---- Expert parallelism (W ranks, each holding experts [r*E/W, (r+1)*E/W) and
+ * calling moe_fp8_block_scale_run with local_expert_offset = r*E/W). The
+ * reference has no multi-GPU path; its only hook is local_expert_offset
+ * (...json:146). These kernels do the data movement around an all-to-all that
+ * the caller runs (NCCL / torch.distributed):
+ *   plan     topk_idx [T, 8] -> send_counts [W] and slot [T, W] (position of a
+ *            token in each destination's block, -1 if that rank owns none of
+ *            its experts); send_counts is cleared first.
+ *   pack     per destination block (offsets = exclusive scan of send_counts):
+ *            logits [S, 256] f32, FP8 rows [S, 7168], scales [S, 56] f32
+ *            (token-major for transport).
+ *   scales   received token-major scales [N, 56] -> [56, N] for the operator.
+ *   combine  partial outputs returned in send order, bf16 [S, 7168] -> output
+ *            [T, 7168] bf16, each token's partials summed in fp32. */
+int moe_fp8_ep_plan(const int32_t* topk_idx, int32_t num_tokens, int32_t world, int32_t experts_per_rank,
+                    int32_t* send_counts, int32_t* slot, void* stream);
+int moe_fp8_ep_pack(const float* routing_logits, const void* hidden_states, const float* hidden_states_scale,
+                    int32_t num_tokens, int32_t world, const int32_t* slot, const int32_t* send_offsets,
+                    float* send_logits, void* send_hidden, float* send_scales, void* stream);
+int moe_fp8_ep_scales(const float* token_major_scales, int32_t num_tokens, float* hidden_states_scale, void* stream);
+int moe_fp8_ep_combine(const void* returned_partials, const int32_t* slot, const int32_t* send_offsets,
+                       int32_t num_tokens, int32_t world, void* output, void* stream);
+
 /* Text of the last error on the calling thread (the reference raises the
  * equivalent message through TVM_FFI_ICHECK, solution/cuda/main.cpp:20-34). */
 const char* moe_fp8_last_error(void);

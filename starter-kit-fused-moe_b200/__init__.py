@@ -67,6 +67,7 @@ EXPORTED_SYMBOLS = (
     "moe_fp8_block_scale_run", "moe_fp8_workspace_bytes", "moe_fp8_route", "moe_fp8_workspace_view",
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
     "moe_fp8_set_gemm_path", "moe_fp8_gemm_path", "moe_fp8_route_static",
+    "moe_fp8_ep_plan", "moe_fp8_ep_pack", "moe_fp8_ep_scales", "moe_fp8_ep_combine",
 )
 
 _lib = None

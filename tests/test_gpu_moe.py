@@ -151,6 +151,14 @@ def test_more_local_experts(pkg, oracle, gpu_inputs):
     assert_close(out.float().cpu().numpy(), ref, what="E=64")
 
 
+def test_all_256_experts_local(pkg, oracle, gpu_inputs):
+    """One device holding every expert (the single-GPU reference of the expert-parallel runs)."""
+    x = gpu_inputs(8, seed=13, E=256)
+    out = pkg.run(*x.args())
+    ref = oracle.moe_forward(*x.args())
+    assert_close(out.float().cpu().numpy(), ref, what="E=256")
+
+
 def test_dps_output_bias_none_and_zero_tokens(pkg, oracle, gpu_inputs):
     x = gpu_inputs(33, seed=3)
     args = list(x.args())
