@@ -202,6 +202,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmA2);
     tma_prefetch_desc(&tmW2);
   }
+  pdl_trigger();
+  pdl_wait();  // the expert histogram and operands come from the preceding kernels
   {
     const int tid = threadIdx.x;
     const int c = tid < E ? args.counts[tid] : 0;
@@ -496,8 +498,8 @@ cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13
     if (e != cudaSuccess) return e;
     if (dev < 64) dec::g_attr_set[dev] = 1;
   }
-  dec::stream_gemm_kernel<<<num_sms, dec::THREADS, dec::SMEM_BYTES, st>>>(tmA1, tmW13, tmA2, tmW2, args);
-  return cudaGetLastError();
+  return launch_kernel(dec::stream_gemm_kernel, dim3(num_sms), dim3(dec::THREADS), dec::SMEM_BYTES, st, true, tmA1, tmW13,
+                       tmA2, tmW2, args);
 }
 
 }  // namespace moe

@@ -173,6 +173,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
+  pdl_trigger();
+  pdl_wait();  // the expert histogram and operands come from the preceding kernels
   // tile list from the device-side expert histogram
   {
     const int tid = threadIdx.x;
@@ -448,8 +450,8 @@ cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
     if (e != cudaSuccess) return e;
     if (dev < 64) g_smem_set[MODE - 1][dev] = 1;
   }
-  grouped_gemm_kernel<MODE><<<num_sms, GEMM_THREADS, GEMM_SMEM_BYTES, st>>>(tmA, tmB, args);
-  return cudaGetLastError();
+  return launch_kernel(grouped_gemm_kernel<MODE>, dim3(num_sms), dim3(GEMM_THREADS), GEMM_SMEM_BYTES, st, true, tmA,
+                       tmB, args);
 }
 
 cudaError_t set_trace(int on) {

@@ -147,7 +147,8 @@ int moe_fp8_route(const float* logits, const void* bias, int32_t T, int32_t offs
   if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
   e = moe::launch_route(logits, static_cast<const __nv_bfloat16*>(bias), T, offset, E, scale,
                         reinterpret_cast<int*>(w + L.topk_idx), reinterpret_cast<float*>(w + L.topk_w),
-                        reinterpret_cast<int*>(w + L.pair_pos), reinterpret_cast<int*>(w + L.counts), nullptr, st);
+                        reinterpret_cast<int*>(w + L.pair_pos), reinterpret_cast<int*>(w + L.counts), nullptr, nullptr,
+                        st);
   if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
   return MOE_OK;
 }
@@ -240,7 +241,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
       e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
                             a->local_expert_offset, E, a->routed_scaling_factor, p.topk_idx, p.topk_w, p.pair_pos,
-                            p.counts, p.acc, st);
+                            p.counts, p.acc, static_cast<__nv_bfloat16*>(a->output), st);
       if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
       break;
     case 1:
@@ -317,7 +318,8 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       break;
     }
     case 4:
-      e = moe::launch_finalize(p.acc, static_cast<__nv_bfloat16*>(a->output), T, p.nsm, st);
+      e = moe::launch_finalize(p.acc, static_cast<__nv_bfloat16*>(a->output), T, p.topk_idx, a->local_expert_offset,
+                               E, p.nsm, st);
       if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
       break;
     default:

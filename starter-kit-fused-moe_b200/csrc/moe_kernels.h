@@ -23,11 +23,12 @@ struct GemmArgs {
 
 cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
                          int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
-                         cudaStream_t st);
+                         __nv_bfloat16* out, cudaStream_t st);
 cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E, int offset, const int* topk_idx,
                            const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
                            float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st);
-cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, int num_sms, cudaStream_t st);
+cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, const int* topk_idx, int offset, int E,
+                            int num_sms, cudaStream_t st);
 // Weight-streaming GEMM kernel (decode_gemm.cu).
 struct DecodeArgs {
   int mode;                // 1: GEMM1 tiles, 2: GEMM2 tiles, 3: both in one launch

@@ -35,9 +35,10 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
     const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, int T, int offset, int E,
     float scale, int* __restrict__ topk_idx, float* __restrict__ topk_w, int* __restrict__ pair_pos,
-    int* __restrict__ counts, float* __restrict__ out_acc) {
+    int* __restrict__ counts, float* __restrict__ out_acc, __nv_bfloat16* __restrict__ out) {
   __shared__ int hist[kMaxLocalExperts];
   __shared__ int base[kMaxLocalExperts];
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
   const int t = blockIdx.x * kRouteWarps + warp;
@@ -135,12 +136,20 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
         my_lpos = atomicAdd(&hist[le], 1);
       }
     }
-    // clear this token's combine accumulator row
+    // A token with a local expert gets a zeroed fp32 combine row (GEMM2 adds into
+    // it, finalize rounds it); a token without one is final already: zero output.
     if (out_acc != nullptr) {
-      float4* row = reinterpret_cast<float4*>(out_acc + (size_t)t * kHidden);
+      const bool has_local = __ballot_sync(0xffffffffu, my_le >= 0) != 0;
       const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (has_local) {
+        float4* row = reinterpret_cast<float4*>(out_acc + (size_t)t * kHidden);
 #pragma unroll 4
-      for (int c = lane; c < kHidden / 4; c += 32) row[c] = z;
+        for (int c = lane; c < kHidden / 4; c += 32) row[c] = z;
+      } else {
+        float4* row = reinterpret_cast<float4*>(out + (size_t)t * kHidden);
+#pragma unroll 4
+        for (int c = lane; c < kHidden / 8; c += 32) row[c] = z;
+      }
     }
   }
   __syncthreads();
@@ -178,6 +187,8 @@ __global__ void __launch_bounds__(256) permute_kernel(
     int* __restrict__ row_token, float* __restrict__ row_weight) {
   __shared__ int off[256];
   __shared__ int warp_sums[8];
+  pdl_wait();
+  pdl_trigger();
   padded_offsets_256(counts, E, off, warp_sums);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
@@ -219,26 +230,35 @@ __global__ void __launch_bounds__(256) permute_kernel(
   }
 }
 
-// out[i] = bf16(acc[i]), 8 elements per thread-iteration.
+// out[t] = bf16(acc[t]) for the tokens with a local expert (the routing kernel
+// already wrote zeros for the others). One warp per token.
 __global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out,
-                                                       size_t n8) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
-    const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
-    const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
-    __nv_bfloat162 r[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
-                           __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
-    reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<uint4*>(r);
+                                                       int T, const int* __restrict__ topk_idx, int offset, int E) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
+    const int le = lane < kTopK ? __ldg(topk_idx + (size_t)t * kTopK + lane) - offset : -1;
+    if (!__ballot_sync(0xffffffffu, le >= 0 && le < E)) continue;
+    const float4* src = reinterpret_cast<const float4*>(acc + (size_t)t * kHidden);
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * kHidden);
+#pragma unroll 4
+    for (int c = lane; c < kHidden / 8; c += 32) {
+      const float4 a = src[2 * c], b = src[2 * c + 1];
+      __nv_bfloat162 r[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                             __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+      dst[c] = *reinterpret_cast<uint4*>(r);
+    }
   }
 }
 
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
                          int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
-                         cudaStream_t st) {
+                         __nv_bfloat16* out, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   const int grid = (T + kRouteWarps - 1) / kRouteWarps;
   route_kernel<<<grid, kRouteWarps * 32, 0, st>>>(logits, bias, T, offset, E, scale, topk_idx, topk_w, pair_pos,
-                                                  counts, out_acc);
+                                                  counts, out_acc, out);
   return cudaGetLastError();
 }
 
@@ -248,18 +268,16 @@ cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E,
   if (T == 0) return cudaSuccess;
   int grid = (T + 7) / 8;
   if (grid > num_sms * 8) grid = num_sms * 8;
-  permute_kernel<<<grid, 256, 0, st>>>(hidden, hs, T, E, offset, topk_idx, topk_w, pair_pos, counts, R1, a1, sa1,
-                                       row_token, row_weight);
-  return cudaGetLastError();
+  return launch_kernel(permute_kernel, dim3(grid), dim3(256), 0, st, true, hidden, hs, T, E, offset, topk_idx, topk_w,
+                       pair_pos, counts, R1, a1, sa1, row_token, row_weight);
 }
 
-cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, int num_sms, cudaStream_t st) {
+cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, const int* topk_idx, int offset, int E,
+                            int num_sms, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  const size_t n8 = (size_t)T * kHidden / 8;
-  size_t grid = (n8 + 255) / 256;
-  if (grid > (size_t)num_sms * 8) grid = (size_t)num_sms * 8;
-  finalize_kernel<<<(unsigned)grid, 256, 0, st>>>(acc, out, n8);
-  return cudaGetLastError();
+  int grid = (T + 7) / 8;
+  if (grid > num_sms * 8) grid = num_sms * 8;
+  return launch_kernel(finalize_kernel, dim3(grid), dim3(256), 0, st, true, acc, out, T, topk_idx, offset, E);
 }
 
 }  // namespace moe

@@ -90,7 +90,7 @@ int moe_fp8_route_static(const float* routing_logits, const void* routing_bias, 
   if (e == cudaSuccess)
     e = moe::launch_route(routing_logits, static_cast<const __nv_bfloat16*>(routing_bias), T, local_expert_offset,
                           E, routed_scaling_factor, topk_idx, topk_weights, scratch + kCounters, scratch, nullptr,
-                          st);
+                          nullptr, st);
   if (e != cudaSuccess)
     return static_fail(MOE_ERR_CUDA, std::string("moe_fp8_route_static: ") + cudaGetErrorString(e));
   return MOE_OK;
