@@ -129,6 +129,14 @@ int moe_fp8_route_static(const float* routing_logits, const void* routing_bias, 
                          int32_t local_expert_offset, int32_t num_local_experts, float routed_scaling_factor,
                          int32_t* topk_idx, float* topk_weights, void* stream);
 
+/* Producer-side activation quantiser: x [T, 7168] (bf16 if x_is_bf16, else f32)
+ * -> hidden_states e4m3 [T, 7168] and hidden_states_scale f32 [56, T], the
+ * operator's input layout (...json:81-88). Per 1x128 block s = max(amax,
+ * 1e-12)/448 and q = e4m3(x/s), round to nearest even. The reference uses the
+ * same recipe to re-quantise the SwiGLU output (cutlass_gemm1_helper.py:189-205). */
+int moe_fp8_quantize_activations(const void* x, int32_t x_is_bf16, int32_t num_tokens, void* hidden_states,
+                                 float* hidden_states_scale, void* stream);
+
 /* ---- Expert parallelism (W ranks, each holding experts [r*E/W, (r+1)*E/W) and
  * calling moe_fp8_block_scale_run with local_expert_offset = r*E/W). The
  * reference has no multi-GPU path; its only hook is local_expert_offset

@@ -84,6 +84,31 @@ def dequant_block(wq: np.ndarray, ws: np.ndarray) -> np.ndarray:
     return (w * ws.astype(np.float32)[:, None, :, None]).reshape(N, K)
 
 
+def e4m3_round(v: np.ndarray) -> np.ndarray:
+    """Round float32 values to the nearest e4m3fn byte (ties to even), saturating at +-448."""
+    v = np.asarray(v, np.float32)
+    finite = E4M3[:127].astype(np.float64)            # bytes 0..126: 0 .. 448, ascending
+    a = np.minimum(np.abs(v).astype(np.float64), 448.0)
+    hi = np.searchsorted(finite, a, side="left").clip(0, 126)
+    lo = (hi - 1).clip(0, 126)
+    dlo, dhi = a - finite[lo], finite[hi] - a
+    pick_hi = (dhi < dlo) | ((dhi == dlo) & (hi % 2 == 0))
+    b = np.where(pick_hi, hi, lo).astype(np.uint8)
+    b = np.where(a == finite[hi], hi, b).astype(np.uint8)
+    return np.where(np.signbit(v), b | 0x80, b).astype(np.uint8)   # sign kept, -0 included
+
+
+def quantize_rows(x: np.ndarray):
+    """x [T, K] -> (e4m3 bytes [T, K], scales f32 [K/128, T]); s = max(amax, 1e-12)/448, q = e4m3(x/s).
+    The activation layout of `...json:81-88` (scales token-contiguous)."""
+    x = np.asarray(x, np.float32)
+    T, K = x.shape
+    xb = x.reshape(T, K // BLOCK, BLOCK)
+    s = (np.maximum(np.abs(xb).max(axis=2), np.float32(1e-12)) / np.float32(448.0)).astype(np.float32)
+    q = e4m3_round((xb / s[:, :, None]).astype(np.float32)).reshape(T, K)
+    return q, s.T.copy()
+
+
 # ---------------------------------------------------------------- routing
 def route(logits: np.ndarray, bias: np.ndarray, routed_scaling_factor: float):
     """Reference step "2) No-aux routing".

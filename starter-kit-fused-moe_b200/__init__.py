@@ -68,6 +68,7 @@ EXPORTED_SYMBOLS = (
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
     "moe_fp8_set_gemm_path", "moe_fp8_gemm_path", "moe_fp8_route_static",
     "moe_fp8_ep_plan", "moe_fp8_ep_pack", "moe_fp8_ep_scales", "moe_fp8_ep_combine",
+    "moe_fp8_quantize_activations",
 )
 
 _lib = None
@@ -266,6 +267,24 @@ def workspace_tensors(ws: torch.Tensor, T: int, E: int):
 
 GEMM_PATHS = {0: "tile kernels", 1: "streaming GEMM1 + tile GEMM2", 2: "fused streaming GEMM1+GEMM2",
               3: "streaming GEMM1 + streaming GEMM2"}
+
+
+@torch.no_grad()
+def quantize_activations(x):
+    """bf16 / f32 [T, 7168] CUDA tensor -> (e4m3 [T, 7168], f32 scales [56, T]), the operator's input layout."""
+    lib = load_library()
+    if x.dim() != 2 or x.shape[1] != H or x.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("x must be bf16 or f32 [T, 7168]")
+    x = x.contiguous()
+    T = int(x.shape[0])
+    q = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(H // 128, T, dtype=torch.float32, device=x.device)
+    lib.moe_fp8_quantize_activations.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                                 ctypes.c_void_p, ctypes.c_void_p]
+    with torch.cuda.device(x.device):
+        _check(lib.moe_fp8_quantize_activations(_ptr(x), int(x.dtype == torch.bfloat16), T, _ptr(q), _ptr(s),
+                                                _stream_handle(x.device)), "moe_fp8_quantize_activations")
+    return q, s
 
 
 def set_gemm_path(path: int) -> int:

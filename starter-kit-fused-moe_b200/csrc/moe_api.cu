@@ -351,6 +351,16 @@ int32_t moe_fp8_set_gemm_path(int32_t path) {
 
 int32_t moe_fp8_gemm_path(int32_t num_tokens) { return gemm_path(num_tokens); }
 
+int moe_fp8_quantize_activations(const void* x, int32_t x_is_bf16, int32_t T, void* hidden_states,
+                                 float* hidden_states_scale, void* stream) {
+  if (T < 0) return fail(MOE_ERR_INVALID_ARGUMENT, "quantize: num_tokens must be >= 0");
+  if (T > 0 && (!x || !hidden_states || !hidden_states_scale || !aligned(x, 16) || !aligned(hidden_states, 16)))
+    return fail(MOE_ERR_INVALID_ARGUMENT, "quantize: NULL or misaligned pointer");
+  cudaError_t e = moe::launch_quantize(x, x_is_bf16 != 0, T, static_cast<uint8_t*>(hidden_states), hidden_states_scale,
+                                       static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOE_OK : cuda_fail(e, "quantize");
+}
+
 int moe_fp8_ep_plan(const int32_t* topk_idx, int32_t T, int32_t world, int32_t experts_per_rank,
                     int32_t* send_counts, int32_t* slot, void* stream) {
   if (T < 0 || world < 1 || world > 64 || experts_per_rank < 1) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_plan: bad sizes");

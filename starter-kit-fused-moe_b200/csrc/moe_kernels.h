@@ -54,6 +54,7 @@ cudaError_t launch_ep_pack(const float* logits, const uint8_t* hidden, const flo
 cudaError_t launch_ep_scales(const float* src, int N, float* dst, cudaStream_t st);
 cudaError_t launch_ep_combine(const __nv_bfloat16* back, const int* slot, const int* send_off, int T, int W,
                               __nv_bfloat16* out, cudaStream_t st);
+cudaError_t launch_quantize(const void* x, bool bf16, int T, uint8_t* q, float* scale, cudaStream_t st);
 // Text returned by moe_fp8_last_error() on the calling thread.
 void set_last_error(const char* msg);
 cudaError_t set_trace(int on);

@@ -231,23 +231,33 @@ __global__ void __launch_bounds__(256) permute_kernel(
 }
 
 // out[t] = bf16(acc[t]) for the tokens with a local expert (the routing kernel
-// already wrote zeros for the others). One warp per token.
+// already wrote zeros for the others). One warp per (token, 1024-column chunk);
+// each lane issues all of its loads before converting.
+constexpr int kFinalizeChunk = 1024;
 __global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out,
                                                        int T, const int* __restrict__ topk_idx, int offset, int E) {
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
-    const int le = lane < kTopK ? __ldg(topk_idx + (size_t)t * kTopK + lane) - offset : -1;
-    if (!__ballot_sync(0xffffffffu, le >= 0 && le < E)) continue;
-    const float4* src = reinterpret_cast<const float4*>(acc + (size_t)t * kHidden);
-    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * kHidden);
-#pragma unroll 4
-    for (int c = lane; c < kHidden / 8; c += 32) {
-      const float4 a = src[2 * c], b = src[2 * c + 1];
-      __nv_bfloat162 r[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
-                             __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
-      dst[c] = *reinterpret_cast<uint4*>(r);
-    }
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const int le = lane < kTopK ? __ldg(topk_idx + (size_t)t * kTopK + lane) - offset : -1;
+  if (!__ballot_sync(0xffffffffu, le >= 0 && le < E)) return;
+  const size_t base = (size_t)t * kHidden + (size_t)blockIdx.y * kFinalizeChunk;
+  const float4* src = reinterpret_cast<const float4*>(acc + base);
+  uint4* dst = reinterpret_cast<uint4*>(out + base);
+  constexpr int kPer = kFinalizeChunk / 8 / 32;  // 4 groups of 8 per lane
+  float4 v[2 * kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    v[2 * i] = __ldg(src + 2 * (lane + 32 * i));
+    v[2 * i + 1] = __ldg(src + 2 * (lane + 32 * i) + 1);
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const float4 a = v[2 * i], b = v[2 * i + 1];
+    __nv_bfloat162 r[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                           __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+    dst[lane + 32 * i] = *reinterpret_cast<uint4*>(r);
   }
 }
 
@@ -275,9 +285,9 @@ cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E,
 cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, const int* topk_idx, int offset, int E,
                             int num_sms, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  int grid = (T + 7) / 8;
-  if (grid > num_sms * 8) grid = num_sms * 8;
-  return launch_kernel(finalize_kernel, dim3(grid), dim3(256), 0, st, true, acc, out, T, topk_idx, offset, E);
+  (void)num_sms;
+  return launch_kernel(finalize_kernel, dim3((T + 7) / 8, kHidden / kFinalizeChunk), dim3(256), 0, st, true, acc, out,
+                       T, topk_idx, offset, E);
 }
 
 }  // namespace moe

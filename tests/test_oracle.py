@@ -74,3 +74,17 @@ def test_tie_aware_selection_helper():
     assert same_selection(np.arange(8)[None], np.arange(8, 16)[None], sb).all()
     sb[0, :8] = 1
     assert not same_selection(np.arange(8)[None], np.arange(8, 16)[None], sb).all()
+
+
+@pytest.mark.parametrize("scale", [1e-3, 1.0, 300.0])
+def test_quantize_restatement_matches_torch(scale, pkg, oracle):
+    """The numpy activation quantiser equals the input generator's torch conversion, bit for bit."""
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(40, 7168, generator=g) * scale
+    x[1, :128] = 0.0                     # all-zero block
+    x[2, 5] = -0.0
+    for xx in (x, x.to(torch.bfloat16).float()):
+        q, s = pkg.inputs.quantize_rows_1x128(xx)
+        q2, s2 = oracle.quantize_rows(xx.numpy())
+        assert np.array_equal(s.numpy(), s2)
+        assert np.array_equal(q.view(torch.uint8).numpy(), q2)
