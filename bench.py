@@ -252,7 +252,7 @@ def run_ep_bench(a, world, rank):
     def step():
         return ep.ep_forward(x.routing_logits, w.routing_bias, x.hidden_states, x.hidden_states_scale,
                              w.gemm1_weights, w.gemm1_weights_scale, w.gemm2_weights, w.gemm2_weights_scale, 2.5,
-                             stats=stats)
+                             stats=stats, waves=a.ep_waves)
 
     for _ in range(a.warmup):
         step()
@@ -275,7 +275,7 @@ def run_ep_bench(a, world, rank):
         for d, h in zip(d_in, h_in):
             d.copy_(h, non_blocking=True)
         o = ep.ep_forward(d_in[0], w.routing_bias, d_in[1], d_in[2], w.gemm1_weights, w.gemm1_weights_scale,
-                          w.gemm2_weights, w.gemm2_weights_scale, 2.5)
+                          w.gemm2_weights, w.gemm2_weights_scale, 2.5, waves=a.ep_waves)
         h_out.copy_(o, non_blocking=True)
 
     e2e_step()
@@ -291,6 +291,7 @@ def run_ep_bench(a, world, rank):
         "config": {"workload": f"expert parallel: {T} tokens per GPU, 256 experts ({epr} per GPU, "
                                f"local_expert_offset = {epr}*rank), NCCL all-to-all dispatch and combine",
                    "tokens_per_rank": T, "experts_per_rank": epr, "parallelism": f"ep{world}",
+                   "waves": a.ep_waves,
                    "sent_tokens_rank0": stats.get("sent_tokens"), "received_tokens_rank0": stats.get("received_tokens"),
                    "l2": "flushed (256 MB write) between timed calls"},
         "tflops": tfl,
@@ -338,6 +339,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="tokens per rank in the multi-GPU (EP) run")
+    ap.add_argument("--ep-waves", type=int, default=1, help="token waves overlapping the EP exchange with compute")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     world, rank, local = dist_setup() if a.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),

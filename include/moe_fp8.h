@@ -140,25 +140,29 @@ int moe_fp8_quantize_activations(const void* x, int32_t x_is_bf16, int32_t num_t
 /* ---- Expert parallelism (W ranks, each holding experts [r*E/W, (r+1)*E/W) and
  * calling moe_fp8_block_scale_run with local_expert_offset = r*E/W). The
  * reference has no multi-GPU path; its only hook is local_expert_offset
- * (...json:146). These kernels do the data movement around an all-to-all that
- * the caller runs (NCCL / torch.distributed):
- *   plan     topk_idx [T, 8] -> send_counts [W] and slot [T, W] (position of a
- *            token in each destination's block, -1 if that rank owns none of
- *            its experts); send_counts is cleared first.
- *   pack     per destination block (offsets = exclusive scan of send_counts):
- *            logits [S, 256] f32, FP8 rows [S, 7168], scales [S, 56] f32
- *            (token-major for transport).
+ * (...json:146). These kernels do the data movement around the all-to-alls
+ * that the caller runs (NCCL / torch.distributed). Tokens are processed in
+ * waves of `wave_tokens` consecutive tokens so that the exchange of one wave
+ * can overlap the grouped GEMMs of another; send blocks are ordered
+ * (wave, destination) and `send_offsets` [waves * W] is the exclusive scan of
+ * `send_counts` in that order.
+ *   plan     topk_idx [T, 8] -> send_counts [waves * W] (cleared first; every
+ *            rank must use the same `waves`, and waves * wave_tokens >= T) and
+ *            slot [T, W] (position of a token in its (wave, destination) block,
+ *            -1 if that rank owns none of its experts).
+ *   pack     logits [S, 256] f32, FP8 rows [S, 7168], scales [S, 56] f32
+ *            (token-major for transport) into the send blocks.
  *   scales   received token-major scales [N, 56] -> [56, N] for the operator.
- *   combine  partial outputs returned in send order, bf16 [S, 7168] -> output
- *            [T, 7168] bf16, each token's partials summed in fp32. */
+ *   combine  partial outputs returned into the send layout, bf16 [S, 7168] ->
+ *            output [T, 7168] bf16, each token's partials summed in fp32. */
 int moe_fp8_ep_plan(const int32_t* topk_idx, int32_t num_tokens, int32_t world, int32_t experts_per_rank,
-                    int32_t* send_counts, int32_t* slot, void* stream);
+                    int32_t wave_tokens, int32_t waves, int32_t* send_counts, int32_t* slot, void* stream);
 int moe_fp8_ep_pack(const float* routing_logits, const void* hidden_states, const float* hidden_states_scale,
                     int32_t num_tokens, int32_t world, const int32_t* slot, const int32_t* send_offsets,
-                    float* send_logits, void* send_hidden, float* send_scales, void* stream);
+                    int32_t wave_tokens, float* send_logits, void* send_hidden, float* send_scales, void* stream);
 int moe_fp8_ep_scales(const float* token_major_scales, int32_t num_tokens, float* hidden_states_scale, void* stream);
 int moe_fp8_ep_combine(const void* returned_partials, const int32_t* slot, const int32_t* send_offsets,
-                       int32_t num_tokens, int32_t world, void* output, void* stream);
+                       int32_t wave_tokens, int32_t num_tokens, int32_t world, void* output, void* stream);
 
 /* Text of the last error on the calling thread (the reference raises the
  * equivalent message through TVM_FFI_ICHECK, solution/cuda/main.cpp:20-34). */

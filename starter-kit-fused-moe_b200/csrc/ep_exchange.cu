@@ -16,12 +16,15 @@ namespace moe {
 
 constexpr int kMaxRanks = 64;
 
-// slot[t * W + d] = position of token t in destination d's send block, -1 if
-// d owns none of t's experts; send_counts[d] = tokens sent to d.
-__global__ void ep_plan_kernel(const int* __restrict__ topk_idx, int T, int W, int experts_per_rank,
+// Tokens are split into waves of `wave_tokens` consecutive tokens; send blocks
+// are ordered (wave, destination). slot[t * W + d] = position of token t in
+// block (wave(t), d), -1 if d owns none of t's experts;
+// send_counts[wave * W + d] = tokens in that block.
+__global__ void ep_plan_kernel(const int* __restrict__ topk_idx, int T, int W, int experts_per_rank, int wave_tokens,
                                int* __restrict__ send_counts, int* __restrict__ slot) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
+  int* counts = send_counts + (size_t)(t / wave_tokens) * W;
   uint64_t mask = 0;
 #pragma unroll
   for (int k = 0; k < kTopK; ++k) {
@@ -29,17 +32,18 @@ __global__ void ep_plan_kernel(const int* __restrict__ topk_idx, int T, int W, i
     if (d >= 0 && d < W) mask |= 1ull << d;
   }
   for (int d = 0; d < W; ++d)
-    slot[(size_t)t * W + d] = ((mask >> d) & 1) ? atomicAdd(&send_counts[d], 1) : -1;
+    slot[(size_t)t * W + d] = ((mask >> d) & 1) ? atomicAdd(&counts[d], 1) : -1;
 }
 
 // Warp per token: copies the token's FP8 row, logits and scales (token-major)
 // into every destination block that needs it.
 __global__ void __launch_bounds__(256) ep_pack_kernel(
     const float* __restrict__ logits, const uint8_t* __restrict__ hidden, const float* __restrict__ hs, int T, int W,
-    const int* __restrict__ slot, const int* __restrict__ send_off, float* __restrict__ s_logits,
+    const int* __restrict__ slot, const int* __restrict__ send_off, int wave_tokens, float* __restrict__ s_logits,
     uint8_t* __restrict__ s_hidden, float* __restrict__ s_scale) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
+    const int* off = send_off + (size_t)(t / wave_tokens) * W;
     constexpr int kPer = kHidden / 16 / 32;  // 14 uint4 per lane
     uint4 v[kPer];
     const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
@@ -52,7 +56,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(
     for (int d = 0; d < W; ++d) {
       const int sl = slot[(size_t)t * W + d];
       if (sl < 0) continue;
-      const size_t row = (size_t)send_off[d] + sl;
+      const size_t row = (size_t)off[d] + sl;
       uint4* dst = reinterpret_cast<uint4*>(s_hidden + row * kHidden);
 #pragma unroll
       for (int i = 0; i < kPer; ++i) dst[lane + 32 * i] = v[i];
@@ -75,10 +79,11 @@ __global__ void ep_scales_kernel(const float* __restrict__ src, int N, float* __
 
 // Warp per token: out[t] = bf16(sum over destinations of the returned partial rows), fp32 sum.
 __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __restrict__ back, const int* __restrict__ slot,
-                                                         const int* __restrict__ send_off, int T, int W,
-                                                         __nv_bfloat16* __restrict__ out) {
+                                                         const int* __restrict__ send_off, int wave_tokens, int T,
+                                                         int W, __nv_bfloat16* __restrict__ out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
+    const int* off = send_off + (size_t)(t / wave_tokens) * W;
     // a token has at most 8 destinations (one per selected expert)
     size_t rows[kTopK];
     int nr = 0;
@@ -87,7 +92,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __
       if (sl >= 0) {
 #pragma unroll
         for (int j = 0; j < kTopK; ++j)
-          if (j == nr) rows[j] = (size_t)send_off[d] + sl;
+          if (j == nr) rows[j] = (size_t)off[d] + sl;
         ++nr;
       }
     }
@@ -116,15 +121,18 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __
   }
 }
 
-cudaError_t launch_ep_plan(const int* topk_idx, int T, int W, int epr, int* send_counts, int* slot, cudaStream_t st) {
+cudaError_t launch_ep_plan(const int* topk_idx, int T, int W, int epr, int wave_tokens, int* send_counts, int* slot,
+                           cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  ep_plan_kernel<<<(T + 255) / 256, 256, 0, st>>>(topk_idx, T, W, epr, send_counts, slot);
+  ep_plan_kernel<<<(T + 255) / 256, 256, 0, st>>>(topk_idx, T, W, epr, wave_tokens, send_counts, slot);
   return cudaGetLastError();
 }
 cudaError_t launch_ep_pack(const float* logits, const uint8_t* hidden, const float* hs, int T, int W, const int* slot,
-                           const int* send_off, float* s_logits, uint8_t* s_hidden, float* s_scale, cudaStream_t st) {
+                           const int* send_off, int wave_tokens, float* s_logits, uint8_t* s_hidden, float* s_scale,
+                           cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  ep_pack_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, hidden, hs, T, W, slot, send_off, s_logits, s_hidden, s_scale);
+  ep_pack_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, hidden, hs, T, W, slot, send_off, wave_tokens, s_logits, s_hidden,
+                                              s_scale);
   return cudaGetLastError();
 }
 cudaError_t launch_ep_scales(const float* src, int N, float* dst, cudaStream_t st) {
@@ -133,10 +141,10 @@ cudaError_t launch_ep_scales(const float* src, int N, float* dst, cudaStream_t s
   ep_scales_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, N, dst);
   return cudaGetLastError();
 }
-cudaError_t launch_ep_combine(const __nv_bfloat16* back, const int* slot, const int* send_off, int T, int W,
-                              __nv_bfloat16* out, cudaStream_t st) {
+cudaError_t launch_ep_combine(const __nv_bfloat16* back, const int* slot, const int* send_off, int wave_tokens, int T,
+                              int W, __nv_bfloat16* out, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  ep_combine_kernel<<<(T + 7) / 8, 256, 0, st>>>(back, slot, send_off, T, W, out);
+  ep_combine_kernel<<<(T + 7) / 8, 256, 0, st>>>(back, slot, send_off, wave_tokens, T, W, out);
   return cudaGetLastError();
 }
 

@@ -361,26 +361,28 @@ int moe_fp8_quantize_activations(const void* x, int32_t x_is_bf16, int32_t T, vo
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "quantize");
 }
 
-int moe_fp8_ep_plan(const int32_t* topk_idx, int32_t T, int32_t world, int32_t experts_per_rank,
-                    int32_t* send_counts, int32_t* slot, void* stream) {
-  if (T < 0 || world < 1 || world > 64 || experts_per_rank < 1) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_plan: bad sizes");
-  if (T > 0 && (!topk_idx || !send_counts || !slot)) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_plan: NULL pointer");
+int moe_fp8_ep_plan(const int32_t* topk_idx, int32_t T, int32_t world, int32_t experts_per_rank, int32_t wave_tokens,
+                    int32_t waves, int32_t* send_counts, int32_t* slot, void* stream) {
+  if (T < 0 || world < 1 || world > 64 || experts_per_rank < 1 || wave_tokens < 1 || waves < 1 ||
+      (long long)wave_tokens * waves < T)
+    return fail(MOE_ERR_INVALID_ARGUMENT, "ep_plan: bad sizes (need waves * wave_tokens >= num_tokens)");
+  if (!send_counts || (T > 0 && (!topk_idx || !slot))) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_plan: NULL pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world, st);
-  if (e == cudaSuccess) e = moe::launch_ep_plan(topk_idx, T, world, experts_per_rank, send_counts, slot, st);
+  cudaError_t e = cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world * waves, st);
+  if (e == cudaSuccess) e = moe::launch_ep_plan(topk_idx, T, world, experts_per_rank, wave_tokens, send_counts, slot, st);
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "ep_plan");
 }
 
 int moe_fp8_ep_pack(const float* routing_logits, const void* hidden_states, const float* hidden_states_scale,
-                    int32_t T, int32_t world, const int32_t* slot, const int32_t* send_offsets, float* send_logits,
-                    void* send_hidden, float* send_scales, void* stream) {
-  if (T < 0 || world < 1 || world > 64) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_pack: bad sizes");
+                    int32_t T, int32_t world, const int32_t* slot, const int32_t* send_offsets, int32_t wave_tokens,
+                    float* send_logits, void* send_hidden, float* send_scales, void* stream) {
+  if (T < 0 || world < 1 || world > 64 || wave_tokens < 1) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_pack: bad sizes");
   if (T > 0 && (!aligned(routing_logits, 16) || !aligned(hidden_states, 16) || !aligned(send_logits, 16) ||
                 !aligned(send_hidden, 16) || !send_scales || !slot || !send_offsets || !hidden_states_scale))
     return fail(MOE_ERR_INVALID_ARGUMENT, "ep_pack: NULL or misaligned pointer");
   cudaError_t e = moe::launch_ep_pack(routing_logits, static_cast<const uint8_t*>(hidden_states), hidden_states_scale,
-                                      T, world, slot, send_offsets, send_logits, static_cast<uint8_t*>(send_hidden),
-                                      send_scales, static_cast<cudaStream_t>(stream));
+                                      T, world, slot, send_offsets, wave_tokens, send_logits,
+                                      static_cast<uint8_t*>(send_hidden), send_scales, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "ep_pack");
 }
 
@@ -391,13 +393,14 @@ int moe_fp8_ep_scales(const float* token_major_scales, int32_t N, float* hidden_
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "ep_scales");
 }
 
-int moe_fp8_ep_combine(const void* returned_partials, const int32_t* slot, const int32_t* send_offsets, int32_t T,
-                       int32_t world, void* output, void* stream) {
-  if (T < 0 || world < 1 || world > 64) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_combine: bad sizes");
+int moe_fp8_ep_combine(const void* returned_partials, const int32_t* slot, const int32_t* send_offsets,
+                       int32_t wave_tokens, int32_t T, int32_t world, void* output, void* stream) {
+  if (T < 0 || world < 1 || world > 64 || wave_tokens < 1) return fail(MOE_ERR_INVALID_ARGUMENT, "ep_combine: bad sizes");
   if (T > 0 && (!aligned(returned_partials, 16) || !aligned(output, 16) || !slot || !send_offsets))
     return fail(MOE_ERR_INVALID_ARGUMENT, "ep_combine: NULL or misaligned pointer");
-  cudaError_t e = moe::launch_ep_combine(static_cast<const __nv_bfloat16*>(returned_partials), slot, send_offsets, T,
-                                         world, static_cast<__nv_bfloat16*>(output), static_cast<cudaStream_t>(stream));
+  cudaError_t e = moe::launch_ep_combine(static_cast<const __nv_bfloat16*>(returned_partials), slot, send_offsets,
+                                         wave_tokens, T, world, static_cast<__nv_bfloat16*>(output),
+                                         static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "ep_combine");
 }
 

@@ -48,12 +48,14 @@ struct DecodeArgs {
 };
 cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13, const CUtensorMap& tmA2,
                                const CUtensorMap& tmW2, const DecodeArgs& args, int num_sms, cudaStream_t st);
-cudaError_t launch_ep_plan(const int* topk_idx, int T, int W, int epr, int* send_counts, int* slot, cudaStream_t st);
+cudaError_t launch_ep_plan(const int* topk_idx, int T, int W, int epr, int wave_tokens, int* send_counts, int* slot,
+                           cudaStream_t st);
 cudaError_t launch_ep_pack(const float* logits, const uint8_t* hidden, const float* hs, int T, int W, const int* slot,
-                           const int* send_off, float* s_logits, uint8_t* s_hidden, float* s_scale, cudaStream_t st);
+                           const int* send_off, int wave_tokens, float* s_logits, uint8_t* s_hidden, float* s_scale,
+                           cudaStream_t st);
 cudaError_t launch_ep_scales(const float* src, int N, float* dst, cudaStream_t st);
-cudaError_t launch_ep_combine(const __nv_bfloat16* back, const int* slot, const int* send_off, int T, int W,
-                              __nv_bfloat16* out, cudaStream_t st);
+cudaError_t launch_ep_combine(const __nv_bfloat16* back, const int* slot, const int* send_off, int wave_tokens, int T,
+                              int W, __nv_bfloat16* out, cudaStream_t st);
 cudaError_t launch_quantize(const void* x, bool bf16, int T, uint8_t* q, float* scale, cudaStream_t st);
 // Text returned by moe_fp8_last_error() on the calling thread.
 void set_last_error(const char* msg);

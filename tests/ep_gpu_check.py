@@ -18,6 +18,7 @@ import __graft_entry__ as ge  # noqa: E402
 
 def main():
     T = int(os.environ.get("EP_CHECK_TOKENS", "200"))
+    waves = int(os.environ.get("EP_CHECK_WAVES", "3"))
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local))
@@ -31,14 +32,14 @@ def main():
     stats = {}
     out = ep.ep_forward(x.routing_logits, full.routing_bias, x.hidden_states, x.hidden_states_scale,
                         full.gemm1_weights[sl], full.gemm1_weights_scale[sl], full.gemm2_weights[sl],
-                        full.gemm2_weights_scale[sl], 2.5, stats=stats)
+                        full.gemm2_weights_scale[sl], 2.5, stats=stats, waves=waves)
     ref = pkg.run(x.routing_logits, full.routing_bias, x.hidden_states, x.hidden_states_scale, full.gemm1_weights,
                   full.gemm1_weights_scale, full.gemm2_weights, full.gemm2_weights_scale, 0, 2.5)
     torch.cuda.synchronize()
     err = (out.float() - ref.float()).abs()
     bad = err > 1e-2 + 2e-2 * ref.float().abs()
     ok = not bool(bad.any()) and pkg.read_device_error() == 0
-    print(f"EP_CHECK rank={rank} world={world} T={T} sent={stats['sent_tokens']} received={stats['received_tokens']} "
+    print(f"EP_CHECK rank={rank} world={world} T={T} waves={waves} sent={stats['sent_tokens']} received={stats['received_tokens']} "
           f"max_abs_err={err.max().item():.3e} bad={int(bad.sum())} ok={ok}", flush=True)
     dist.barrier()
     dist.destroy_process_group()

@@ -29,17 +29,18 @@ class TorchExchange:
         idx, _ = self.O.route(logits.numpy(), bias.float().numpy(), scale)
         return torch.from_numpy(idx.astype(np.int32))
 
-    def plan(self, topk_idx, world, epr):
+    def plan(self, topk_idx, world, epr, wave_tokens, waves):
         T = topk_idx.shape[0]
-        counts = torch.zeros(world, dtype=torch.int32)
+        counts = torch.zeros(waves * world, dtype=torch.int32)
         slot = torch.full((T, world), -1, dtype=torch.int32)
         for t in range(T):
             for d in sorted({int(e) // epr for e in topk_idx[t]}):
-                slot[t, d] = counts[d]
-                counts[d] += 1
+                c = (t // wave_tokens) * world + d
+                slot[t, d] = counts[c]
+                counts[c] += 1
         return counts, slot
 
-    def pack(self, logits, hidden, hs, slot, send_off, total):
+    def pack(self, logits, hidden, hs, slot, send_off, total, wave_tokens):
         s_logits = torch.empty(total, 256)
         s_hidden = torch.empty(total, H, dtype=torch.uint8)
         s_scale = torch.empty(total, 56)
@@ -47,7 +48,7 @@ class TorchExchange:
         for t in range(T):
             for d in range(W):
                 if slot[t, d] >= 0:
-                    r = int(send_off[d] + slot[t, d])
+                    r = int(send_off[(t // wave_tokens) * W + d] + slot[t, d])
                     s_logits[r] = logits[t]
                     s_hidden[r] = hidden[t].view(torch.uint8)
                     s_scale[r] = hs[:, t]
@@ -63,13 +64,13 @@ class TorchExchange:
         coef = (w * (idx + 1) * loc).sum(1) * (1.0 + hidden_u8.float().mean(1).numpy())
         return torch.from_numpy(coef).float()[:, None].expand(-1, H).to(torch.bfloat16).contiguous()
 
-    def combine(self, back, slot, send_off, T):
+    def combine(self, back, slot, send_off, T, wave_tokens):
         out = torch.zeros(T, H)
         W = slot.shape[1]
         for t in range(T):
             for d in range(W):
                 if slot[t, d] >= 0:
-                    out[t] += back[int(send_off[d] + slot[t, d])].float()
+                    out[t] += back[int(send_off[(t // wave_tokens) * W + d] + slot[t, d])].float()
         return out.to(torch.bfloat16)
 
 
@@ -81,7 +82,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, result_q):
+def _worker(rank, world, port, result_q, waves):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -100,7 +101,7 @@ def _worker(rank, world, port, result_q):
         w13 = torch.zeros(epr, 1, 1)                       # shapes only matter for the expert count
         stats = {}
         out = ep.ep_forward(logits, bias, hidden, hs, w13, None, None, None, 2.5, backend=TorchExchange(O),
-                            stats=stats)
+                            stats=stats, waves=waves)
         idx, w = O.route(logits.numpy(), bias.float().numpy(), 2.5)
         want = (w * (idx + 1)).sum(1) * (1.0 + hidden.view(torch.uint8).float().mean(1).numpy())
         got = out.float()[:, 0].numpy()
@@ -110,12 +111,12 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_orchestration_gloo(world):
+@pytest.mark.parametrize("world,waves", [(2, 1), (2, 3), (4, 2), (2, 20)])   # 20 waves: some empty
+def test_ep_orchestration_gloo(world, waves):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, waves)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in range(world)]
