@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int i = 0; i < NTOK; ++i) {
           const float x1 = g[i], x2 = u[i];
-          g[i] = (x2 / (1.0f + expf(-x2))) * x1;
+          g[i] = silu_mul(x1, x2);
           am[i] = fabsf(g[i]);
         }
 #pragma unroll

@@ -34,9 +34,12 @@
 
 namespace moe {
 
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
-constexpr int A_TILE = BM * BK;  // 16 KB
-constexpr int B_TILE = BN * BK;  // 32 KB
+// Tiles are 128 rows x 256 columns; scales change every BK = 128 of K, but the
+// shared-memory ring moves SK = 64 of K per stage (64-byte swizzle), so nine
+// 24 KB stages keep more bytes in flight while the MMA holds one of them.
+constexpr int BM = 128, BN = 256, BK = 128, SK = 64, STAGES = 9;
+constexpr int A_TILE = BM * SK;  // 8 KB
+constexpr int B_TILE = BN * SK;  // 16 KB
 constexpr int STAGE_BYTES = A_TILE + B_TILE;
 constexpr int GEMM_THREADS = 320;
 constexpr int EPI_WARPS = 8;
@@ -54,22 +57,24 @@ struct GemmSmem {
   int total_tiles;
   int warp_sums[8];
   int tile_start[kMaxLocalExperts + 1];
-  int mt_cnt[kMaxLocalExperts];
   int row_off[kMaxLocalExperts];
   int cnt[kMaxLocalExperts];
   float amax_x[2][2][BM];
 };
 constexpr size_t GEMM_SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(GemmSmem);
+static_assert(GEMM_SMEM_BYTES <= 232448, "shared memory budget");
 
 // Optional timeline of CTA 0 (clock64 per K-block and role), enabled by
 // moe_fp8_set_trace(1); slots: 0 promotion wait start, 1 wait end, 2 promotion
-// end, 3 MMA wait start, 4 MMA issued, 5 producer slot acquired.
-constexpr int kTraceKBlocks = 512;
-__device__ unsigned long long g_trace[kTraceKBlocks * 8];
+// end, 3 MMA wait start, 4 MMA issued, 5 producer slot acquired, 6/7 tile-end
+// work start/end (at the tile's last K-block), 8 SwiGLU done, 9 row amax
+// exchanged, 10 stores issued.
+constexpr int kTraceKBlocks = 512, kTraceSlots = 16;
+__device__ unsigned long long g_trace[kTraceKBlocks * kTraceSlots];
 __device__ int g_trace_on;
 
 __device__ __forceinline__ void trace_mark(int kt, int slot) {
-  if (blockIdx.x == 0 && kt < kTraceKBlocks && g_trace_on) g_trace[kt * 8 + slot] = clock64();
+  if (blockIdx.x == 0 && kt < kTraceKBlocks && g_trace_on) g_trace[kt * kTraceSlots + slot] = clock64();
 }
 
 template <int MODE>
@@ -112,7 +117,8 @@ __device__ __forceinline__ int block_scan_256(int v, int* warp_sums, int& total)
   return pre + inc - v;
 }
 
-__device__ __forceinline__ void decode_tile(const GemmSmem& S, int E, int t, int& e, int& nt, int& mt) {
+__device__ __forceinline__ void decode_tile(const GemmSmem& S, int E, int rows_per_pair, int t, int& e, int& nt,
+                                            int& mt) {
   int lo = 0, hi = E - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -121,7 +127,7 @@ __device__ __forceinline__ void decode_tile(const GemmSmem& S, int E, int t, int
   }
   e = lo;
   const int local = t - S.tile_start[e];
-  const int m = S.mt_cnt[e];
+  const int m = (S.cnt[e] * rows_per_pair + BM - 1) / BM;
   nt = local / m;
   mt = local - nt * m;
 }
@@ -185,7 +191,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int tstart = block_scan_256(mt * NT, S.warp_sums, tot1);
     if (tid < E) {
       S.cnt[tid] = c;
-      S.mt_cnt[tid] = mt;
       S.row_off[tid] = roff;
       S.tile_start[tid] = tstart;
     }
@@ -211,9 +216,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
         int e, nt, mt;
-        decode_tile(S, E, t, e, nt, mt);
+        decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
         const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int ks = 0; ks < KB * (BK / SK); ++ks, ++it) {   // 64-wide K steps
           const int s = it % STAGES, u = it / STAGES;
           if (!mbar_wait(smem_u32(&S.empty[s]), (u & 1) ^ 1)) {
             set_abort(S, args.err, kErrTimeoutProducer);
@@ -224,13 +229,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t fb = smem_u32(&S.full[s]);
           const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_TILE;
+          const int x = ks * SK;
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
-          tma_load_2d(sa, &tmA, fb, kb * BK, arow);
+          tma_load_2d(sa, &tmA, fb, x, arow);
           if (MODE == 1) {
-            tma_load_2d(sb, &tmB, fb, kb * BK, e * kGemm1N + nt * 128);
-            tma_load_2d(sb + B_TILE / 2, &tmB, fb, kb * BK, e * kGemm1N + kInter + nt * 128);
+            tma_load_2d(sb, &tmB, fb, x, e * kGemm1N + nt * 128);
+            tma_load_2d(sb + B_TILE / 2, &tmB, fb, x, e * kGemm1N + kInter + nt * 128);
           } else {
-            tma_load_2d(sb, &tmB, fb, kb * BK, e * kHidden + nt * BN);
+            tma_load_2d(sb, &tmB, fb, x, e * kHidden + nt * BN);
           }
         }
       }
@@ -242,23 +248,31 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int it = 0, kt = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
-        for (int kb = 0; kb < KB; ++kb, ++it, ++kt) {
-          const int s = it % STAGES, u = it / STAGES;
+        for (int kb = 0; kb < KB && ok; ++kb, ++kt) {
           const int b = kt & 1, v = kt >> 1;
           trace_mark(kt, 3);
-          if (!mbar_wait(smem_u32(&S.tempty[b]), (v & 1) ^ 1) || !mbar_wait(smem_u32(&S.full[s]), u & 1)) {
+          if (!mbar_wait(smem_u32(&S.tempty[b]), (v & 1) ^ 1)) {
             set_abort(S, args.err, kErrTimeoutMma);
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(b * BN);
-          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t sb = sa + A_TILE;
+          for (int h = 0; h < BK / SK; ++h, ++it) {           // two 64-wide stages per scale block
+            const int s = it % STAGES, u = it / STAGES;
+            if (!mbar_wait(smem_u32(&S.full[s]), u & 1)) {
+              set_abort(S, args.err, kErrTimeoutMma);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+            const uint32_t sb = sa + A_TILE;
 #pragma unroll
-          for (int kk = 0; kk < BK / 32; ++kk)
-            mma_e4m3(d, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc, kk > 0 ? 1u : 0u);
-          mma_commit(smem_u32(&S.empty[s]));
+            for (int kk = 0; kk < SK / 32; ++kk)
+              mma_e4m3(d, sdesc_sw64(sa + kk * 32), sdesc_sw64(sb + kk * 32), idesc, (h | kk) ? 1u : 0u);
+            mma_commit(smem_u32(&S.empty[s]));
+          }
+          if (!ok) break;
           mma_commit(smem_u32(&S.tfull[b]));
           trace_mark(kt, 4);
         }
@@ -271,36 +285,59 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int g = ew >> 2;           // column half
     const int r = 32 * q + lane;     // row inside the tile
     const uint32_t lane_addr = tmem_base + ((uint32_t)(32 * q) << 16);
+    // Per-tile epilogue state. The next tile's state (its block-scale pointers
+    // and first kScalePrefetch scales) is loaded before the current tile's
+    // output work, so those global-load latencies overlap that work.
+    constexpr int PF = kScalePrefetch;
+    static_assert(KB % PF == 0, "K-blocks must be a multiple of the prefetch depth");
+    struct TileState {
+      int e, nt, row_in_expert, arow;
+      bool valid;
+      const float* sbp;
+      const float* sbp2;
+      float sa_r[PF], sb_r[PF], sb2_r[PF];
+    };
+    const size_t ld_sa = (size_t)Cfg::ROWS_PER_PAIR * args.R1;
+    auto load_state = [&](int t, TileState& ts) {
+      int mt;
+      decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, ts.e, ts.nt, mt);
+      ts.row_in_expert = mt * BM + r;                         // GEMM row inside the expert's group
+      ts.arow = Cfg::ROWS_PER_PAIR * S.row_off[ts.e] + ts.row_in_expert;
+      ts.valid = ts.row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[ts.e];
+      if (MODE == 1) {
+        ts.sbp = args.sb + ((size_t)ts.e * 32 + ts.nt) * kHiddenBlocks;        // gate block row
+        ts.sbp2 = args.sb + ((size_t)ts.e * 32 + 16 + ts.nt) * kHiddenBlocks;  // up block row
+      } else {
+        ts.sbp = args.sb + ((size_t)ts.e * kHiddenBlocks + 2 * ts.nt + g) * kInterBlocks;
+        ts.sbp2 = nullptr;
+      }
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        ts.sa_r[u] = __ldg(args.sa + (size_t)u * ld_sa + ts.arow);
+        ts.sb_r[u] = __ldg(ts.sbp + u);
+        ts.sb2_r[u] = MODE == 1 ? __ldg(ts.sbp2 + u) : 0.f;
+      }
+    };
+    TileState cur, nxt;
+    if (blockIdx.x < total) load_state(blockIdx.x, nxt);
     int kt = 0, tile_iter = 0;
     for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++tile_iter) {
-      int e, nt, mt;
-      decode_tile(S, E, t, e, nt, mt);
-      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
-      const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + row_in_expert;
-      const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
-      const size_t ld_sa = (size_t)Cfg::ROWS_PER_PAIR * args.R1;
-      // weight block scales for this tile
-      const float* sbp;
-      const float* sbp2 = nullptr;
-      if (MODE == 1) {
-        sbp = args.sb + ((size_t)e * 32 + nt) * kHiddenBlocks;           // gate block row
-        sbp2 = args.sb + ((size_t)e * 32 + 16 + nt) * kHiddenBlocks;     // up block row
-      } else {
-        sbp = args.sb + ((size_t)e * kHiddenBlocks + 2 * nt + g) * kInterBlocks;
-      }
+      cur = nxt;
+      const int e = cur.e, nt = cur.nt, row_in_expert = cur.row_in_expert, arow = cur.arow;
+      const bool valid = cur.valid;
+      const float* sbp = cur.sbp;
+      const float* sbp2 = cur.sbp2;
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
       // Block scales are prefetched kScalePrefetch K-blocks ahead in a register
       // ring, so no global-load latency sits on the per-K-block critical path.
-      constexpr int PF = kScalePrefetch;
-      static_assert(KB % PF == 0, "K-blocks must be a multiple of the prefetch depth");
       float sa_r[PF], sb_r[PF], sb2_r[PF];
 #pragma unroll
       for (int u = 0; u < PF; ++u) {
-        sa_r[u] = __ldg(args.sa + (size_t)u * ld_sa + arow);
-        sb_r[u] = __ldg(sbp + u);
-        sb2_r[u] = MODE == 1 ? __ldg(sbp2 + u) : 0.f;
+        sa_r[u] = cur.sa_r[u];
+        sb_r[u] = cur.sb_r[u];
+        sb2_r[u] = cur.sb2_r[u];
       }
       bool ok = true;
       for (int kb0 = 0; kb0 < KB && ok; kb0 += PF) {
@@ -347,17 +384,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
       if (!ok) break;
+      if (warp == 4 && lane == 0) trace_mark(kt - 1, 6);
+      if (t + (int)gridDim.x < total) load_state(t + gridDim.x, nxt);
 
       if (MODE == 1) {
         // SwiGLU: C = silu(X2) * X1 with X1 = gate half (cols < I), X2 = up half
         float amax = 0.f;
+        if (valid) {                     // rows past the expert's count hold no data
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float x1 = acc[j], x2 = acc[64 + j];
-          const float c = (x2 / (1.0f + expf(-x2))) * x1;
-          acc[j] = c;
-          amax = fmaxf(amax, fabsf(c));
+          for (int j = 0; j < 64; ++j) {
+            const float c = silu_mul(acc[j], acc[64 + j]);
+            acc[j] = c;
+            amax = fmaxf(amax, fabsf(c));
+          }
         }
+        if (warp == 4 && lane == 0) trace_mark(kt - 1, 8);
         // exchange the row maximum with the warp that holds the other 64 columns
         const int xb = tile_iter & 1;
         S.amax_x[xb][g][r] = amax;
@@ -368,6 +409,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           break;
         }
         amax = fmaxf(amax, S.amax_x[xb][g ^ 1][r]);
+        if (warp == 4 && lane == 0) trace_mark(kt - 1, 9);
         if (valid) {
           const float s_hi = amax / kFp8Max;
           const float inv_hi = amax > 0.f ? kFp8Max / amax : 0.f;
@@ -393,6 +435,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             reinterpret_cast<uint4*>(dhi)[k] = make_uint4(hi[4 * k], hi[4 * k + 1], hi[4 * k + 2], hi[4 * k + 3]);
             reinterpret_cast<uint4*>(dlo)[k] = make_uint4(lo[4 * k], lo[4 * k + 1], lo[4 * k + 2], lo[4 * k + 3]);
           }
+          if (warp == 4 && lane == 0) trace_mark(kt - 1, 10);
           if (g == 0) {
             float* sa2 = args.sa2 + (size_t)nt * 2 * args.R1 + 2 * prow;
             sa2[0] = s_hi;
@@ -426,6 +469,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (valid) atomicAdd(reinterpret_cast<float4*>(dst) + j4, make_float4(o[0], o[1], o[2], o[3]));
         }
       }
+      if (warp == 4 && lane == 0) trace_mark(kt - 1, 7);
     }
   }
 
@@ -457,13 +501,13 @@ cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
 cudaError_t set_trace(int on) {
   cudaError_t e = cudaMemcpyToSymbol(g_trace_on, &on, sizeof(int));
   if (e == cudaSuccess && on) {
-    static unsigned long long zeros[kTraceKBlocks * 8];
+    static unsigned long long zeros[kTraceKBlocks * kTraceSlots];
     e = cudaMemcpyToSymbol(g_trace, zeros, sizeof(zeros));
   }
   return e;
 }
 cudaError_t read_trace(unsigned long long* host, int n) {
-  if (n > kTraceKBlocks * 8) n = kTraceKBlocks * 8;
+  if (n > kTraceKBlocks * kTraceSlots) n = kTraceKBlocks * kTraceSlots;
   return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * n);
 }
 

@@ -49,16 +49,18 @@ EncodeTiledFn get_encode_fn() {
 }
 
 // 2-D byte tensor [rows, cols] (row-major), tile box [box_rows, 128 bytes], 128-byte swizzle.
-bool encode_fp8_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+bool encode_fp8_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows,
+                   uint32_t box_cols = 128) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -223,10 +225,12 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
   p.path = gemm_path(T);
   const bool s1 = p.path != 0, s2 = p.path >= 2;
   const uint32_t w2_box = s2 ? 128 : 256;
-  if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, s1 ? 16 : 128) ||
-      !encode_fp8_2d(&p.tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128) ||
-      !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, s2 ? 16 : 128) ||
-      !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, w2_box))
+  // streaming kernels: 128-byte boxes, 128-byte swizzle; tile kernels: 64-byte boxes, 64-byte swizzle
+  const uint32_t c1 = s1 ? 128 : 64, c2 = s2 ? 128 : 64;
+  if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, s1 ? 16 : 128, c1) ||
+      !encode_fp8_2d(&p.tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128, c1) ||
+      !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, s2 ? 16 : 128, c2) ||
+      !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, w2_box, c2))
     return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   return MOE_OK;
 }

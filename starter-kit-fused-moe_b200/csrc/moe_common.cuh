@@ -143,6 +143,25 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
   return d;
 }
 
+// SwiGLU of one intermediate column: silu(x2) * x1 = x2 / (1 + e^-x2) * x1,
+// with the hardware exponential and the approximate division (a few ulp; for
+// x2 -> -inf the quotient goes to 0, for x2 -> +inf it is x2).
+__device__ __forceinline__ float silu_mul(float x1, float x2) {
+  return __fdividef(x2, 1.0f + __expf(-x2)) * x1;
+}
+
+// Same for the 64-byte swizzle canonical layout: rows of 64 bytes, 8-row core
+// groups 512 bytes apart, layout type 4 (SW64); tiles 512-byte aligned.
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;              // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(512 >> 4) << 32;     // SBO
+  d |= (uint64_t)1 << 46;              // version
+  d |= (uint64_t)4 << 61;              // SWIZZLE_64B
+  return d;
+}
+
 // Instruction descriptor for kind::f8f6f4 with e4m3 A and B, f32 accumulator,
 // both operands K-major. N>>3 at [17,23), M>>4 at [24,29).
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
