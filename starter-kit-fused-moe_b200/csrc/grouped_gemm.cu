@@ -10,16 +10,20 @@
 // One persistent CTA per SM walks a device-built tile list
 // (expert, n-tile, m-tile), so no host synchronisation is needed for the
 // expert histogram. Inside a CTA, warps specialise:
-//   warp 0      TMA producer: A tile 128x128 and B tile 256x128 (FP8, 128-byte
-//               swizzle) per K-block into a 4-stage shared-memory ring;
+//   warp 0      TMA producer: A tile 128xSK and B tile 256xSK (FP8, swizzled)
+//               per stage into a shared-memory ring (SK = 128: 48 KB stages);
 //   warp 1      allocates 512 TMEM columns and issues tcgen05.mma kind::f8f6f4
-//               (M=128, N=256, 4 x K=32 per K-block) into one of two TMEM
-//               partial accumulators;
+//               (M=128, N=256, K=32 steps) into one of two TMEM partial
+//               accumulators, one partial per 128-wide K-block;
+//   warp 11     copies the block scales into shared memory with cp.async
+//               (a ring of per-K-block activation-scale slices and per-tile
+//               weight-scale rows, plus GEMM2's pair tokens and weights);
 //   warps 2-9   promote every K-block's partial into registers with its block
 //               scales (acc += partial * sa[row, kb] * sb[n-block, kb]): the
 //               scales differ per K-block, so they are applied here, exactly
 //               once per 128-wide K-block, while the tensor core already runs
-//               the next K-block into the other TMEM buffer.
+//               the next K-block into the other TMEM buffer;
+//   warp 10     (GEMM2) issues the output reductions the epilogue staged.
 // Epilogues:
 //   GEMM1  SwiGLU, then the 128 outputs of a row are re-quantised to FP8 as
 //          two terms (hi = e4m3(c/s), lo = e4m3((c - hi*s)/(s/16)), s = amax/448)
@@ -27,31 +31,46 @@
 //          own 1x128 scale; GEMM2 sums the pair, so the intermediate keeps
 //          about 8 bits of precision while GEMM2 stays on FP8 MMA.
 //   GEMM2  sums the hi/lo rows (lane pair shuffle), multiplies by the routing
-//          weight and adds into the fp32 token accumulator (vector atomics):
-//          the top-k combine happens here, with no separate reduce pass.
+//          weight and stages the 128-column rows in shared memory; warp 10
+//          adds them to the fp32 token accumulator with asynchronous bulk
+//          reductions (cp.reduce.async.bulk .add.f32), so the top-k combine
+//          happens here, with no separate reduce pass, and overlaps the next
+//          tile's main loop.
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 
 namespace moe {
 
-// Tiles are 128 rows x 256 columns; scales change every BK = 128 of K, but the
-// shared-memory ring moves SK = 64 of K per stage (64-byte swizzle), so nine
-// 24 KB stages keep more bytes in flight while the MMA holds one of them.
-constexpr int BM = 128, BN = 256, BK = 128, SK = 64, STAGES = 9;
-constexpr int A_TILE = BM * SK;  // 8 KB
-constexpr int B_TILE = BN * SK;  // 16 KB
-constexpr int STAGE_BYTES = A_TILE + B_TILE;
-constexpr int GEMM_THREADS = 320;
+// Tiles are 128 rows x 256 columns; block scales change every BK = 128 of K.
+// Each GEMM's shared-memory ring moves SK (kTileStageK1/2) of K per stage.
+constexpr int BM = 128, BN = 256, BK = 128, MAX_STAGES = 8;
+// warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 promotion + epilogue,
+// warp 10 GEMM2's output-reduction issuer, warp 11 block-scale loader
+constexpr int GEMM_THREADS = 384;
+constexpr int STORE_WARP = 10;
+constexpr int SCALE_WARP = 11;
 constexpr int EPI_WARPS = 8;
 constexpr int TMEM_COLS = 512;
-constexpr int kScalePrefetch = 2;
+constexpr int kScaleRing = 8;        // K-blocks of activation scales in flight
 
 struct GemmSmem {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[MAX_STAGES];
+  uint64_t empty[MAX_STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t amax_bar[2];
+  uint64_t staged[EPI_WARPS];   // GEMM2: an epilogue warp's rows are staged
+  uint64_t sfree[EPI_WARPS];    // GEMM2: the store warp has read them
+  int row_tok[EPI_WARPS][16];   // GEMM2: token of each staged row, -1 if none
+  uint64_t scfull[kScaleRing];  // activation-scale ring (one 128-row slice per K-block)
+  uint64_t scempty[kScaleRing];
+  uint64_t tbfull[2];           // per-tile weight scales (+ GEMM2 pair tokens and weights)
+  uint64_t tbempty[2];
+  alignas(16) float sa_ring[kScaleRing][BM];
+  // GEMM1: [0,56) gate-row scales, [64,120) up-row scales.
+  // GEMM2: [0,32) scales of output column blocks 2nt and 2nt+1, [64,128) the
+  // tile's 64 pair tokens (int), [128,192) their routing weights.
+  alignas(16) float tile_buf[2][192];
   uint32_t tmem_base;
   int abort_flag;
   int total_tiles;
@@ -61,14 +80,13 @@ struct GemmSmem {
   int cnt[kMaxLocalExperts];
   float amax_x[2][2][BM];
 };
-constexpr size_t GEMM_SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(GemmSmem);
-static_assert(GEMM_SMEM_BYTES <= 232448, "shared memory budget");
 
 // Optional timeline of CTA 0 (clock64 per K-block and role), enabled by
 // moe_fp8_set_trace(1); slots: 0 promotion wait start, 1 wait end, 2 promotion
 // end, 3 MMA wait start, 4 MMA issued, 5 producer slot acquired, 6/7 tile-end
 // work start/end (at the tile's last K-block), 8 SwiGLU done, 9 row amax
-// exchanged, 10 stores issued.
+// exchanged, 10 stores issued (GEMM2: 8 next tile's state loaded, 9 staging
+// free, 10 staged, 11 fenced).
 constexpr int kTraceKBlocks = 512, kTraceSlots = 16;
 __device__ unsigned long long g_trace[kTraceKBlocks * kTraceSlots];
 __device__ int g_trace_on;
@@ -84,13 +102,35 @@ struct GemmCfg<1> {
   static constexpr int KB = kHiddenBlocks;   // 56 K-blocks over H
   static constexpr int NT = kInter / 128;    // 16 n-tiles: 128 gate + 128 up columns each
   static constexpr int ROWS_PER_PAIR = 1;
+  static constexpr int SK = kTileStageK1;
+  static constexpr int STAGES = SK == 128 ? 4 : 8;
+  static constexpr int STAGING = 0;
 };
 template <>
 struct GemmCfg<2> {
   static constexpr int KB = kInterBlocks;    // 16 K-blocks over I
   static constexpr int NT = kHidden / BN;    // 28 n-tiles of 256 output columns
   static constexpr int ROWS_PER_PAIR = 2;    // hi and lo term rows
+  static constexpr int SK = kTileStageK2;
+  static constexpr int STAGES = SK == 128 ? 3 : 6;
+  // per epilogue warp: 16 output rows of 128 fp32 (512 B), 528 B apart so the
+  // float4 writes of 8 consecutive lanes fall in at most 2-way bank conflicts
+  static constexpr int ROW_STRIDE = 528;
+  static constexpr int STAGING = EPI_WARPS * 16 * ROW_STRIDE;
 };
+
+template <int MODE>
+constexpr int stage_bytes() {
+  return (BM + BN) * GemmCfg<MODE>::SK;
+}
+template <int MODE>
+constexpr size_t gemm_smem_bytes() {
+  return 1024 + (size_t)GemmCfg<MODE>::STAGES * stage_bytes<MODE>() + GemmCfg<MODE>::STAGING + sizeof(GemmSmem);
+}
+static_assert(gemm_smem_bytes<1>() <= 232448 && gemm_smem_bytes<2>() <= 232448, "shared memory budget");
+static_assert(GemmCfg<1>::STAGES <= MAX_STAGES && GemmCfg<2>::STAGES <= MAX_STAGES, "barrier arrays");
+static_assert((GemmCfg<1>::SK == 128 || GemmCfg<1>::SK == 64) && (GemmCfg<2>::SK == 128 || GemmCfg<2>::SK == 64),
+              "stage K width");
 
 // Block-wide exclusive scan of one int per thread over threads < 256.
 __device__ __forceinline__ int block_scan_256(int v, int* warp_sums, int& total) {
@@ -155,10 +195,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmArgs args) {
   using Cfg = GemmCfg<MODE>;
-  constexpr int KB = Cfg::KB, NT = Cfg::NT;
+  constexpr int KB = Cfg::KB, NT = Cfg::NT, STAGES = Cfg::STAGES, SK = Cfg::SK, HS = BK / SK;
+  constexpr int A_TILE = BM * SK, B_TILE = BN * SK, STAGE_BYTES = A_TILE + B_TILE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  GemmSmem& S = *reinterpret_cast<GemmSmem*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  GemmSmem& S = *reinterpret_cast<GemmSmem*>(staging + Cfg::STAGING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = args.E;
 
@@ -171,6 +213,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(smem_u32(&S.tfull[b]), 1);
       mbar_init(smem_u32(&S.tempty[b]), EPI_WARPS);
       mbar_init(smem_u32(&S.amax_bar[b]), EPI_WARPS);
+    }
+    for (int w = 0; w < EPI_WARPS; ++w) {
+      mbar_init(smem_u32(&S.staged[w]), 1);
+      mbar_init(smem_u32(&S.sfree[w]), 1);
+    }
+    for (int i = 0; i < kScaleRing; ++i) {
+      mbar_init(smem_u32(&S.scfull[i]), 32);     // one cp.async arrival per loader lane
+      mbar_init(smem_u32(&S.scempty[i]), EPI_WARPS);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&S.tbfull[b]), 32);
+      mbar_init(smem_u32(&S.tbempty[b]), EPI_WARPS);
     }
     S.abort_flag = 0;
     fence_barrier_init();
@@ -218,7 +272,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         int e, nt, mt;
         decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
         const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
-        for (int ks = 0; ks < KB * (BK / SK); ++ks, ++it) {   // 64-wide K steps
+        for (int ks = 0; ks < KB * HS; ++ks, ++it) {
           const int s = it % STAGES, u = it / STAGES;
           if (!mbar_wait(smem_u32(&S.empty[s]), (u & 1) ^ 1)) {
             set_abort(S, args.err, kErrTimeoutProducer);
@@ -257,7 +311,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           const uint32_t d = tmem_base + (uint32_t)(b * BN);
-          for (int h = 0; h < BK / SK; ++h, ++it) {           // two 64-wide stages per scale block
+          for (int h = 0; h < HS; ++h, ++it) {                // HS stages per scale block
             const int s = it % STAGES, u = it / STAGES;
             if (!mbar_wait(smem_u32(&S.full[s]), u & 1)) {
               set_abort(S, args.err, kErrTimeoutMma);
@@ -268,8 +322,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
             const uint32_t sb = sa + A_TILE;
 #pragma unroll
-            for (int kk = 0; kk < SK / 32; ++kk)
-              mma_e4m3(d, sdesc_sw64(sa + kk * 32), sdesc_sw64(sb + kk * 32), idesc, (h | kk) ? 1u : 0u);
+            for (int kk = 0; kk < SK / 32; ++kk) {
+              const uint64_t da = SK == 128 ? sdesc_sw128(sa + kk * 32) : sdesc_sw64(sa + kk * 32);
+              const uint64_t db = SK == 128 ? sdesc_sw128(sb + kk * 32) : sdesc_sw64(sb + kk * 32);
+              mma_e4m3(d, da, db, idesc, (h | kk) ? 1u : 0u);
+            }
             mma_commit(smem_u32(&S.empty[s]));
           }
           if (!ok) break;
@@ -278,6 +335,86 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
     }
+  } else if (warp == SCALE_WARP) {
+    // ------------------------------------------------------------ block-scale loader
+    // Copies, with 16-byte cp.async whose completion the mbarriers track, each
+    // K-block's 128 activation scales into a ring and per tile the weight-scale
+    // rows (GEMM2 also the tile's pair tokens and routing weights), so the
+    // epilogue reads every scale from shared memory.
+    const size_t ld_sa = (size_t)Cfg::ROWS_PER_PAIR * args.R1;
+    int kq = 0, j = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x, ++j) {
+      int e, nt, mt;
+      decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
+      const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
+      const int tb = j & 1;
+      if (!mbar_wait(smem_u32(&S.tbempty[tb]), ((j >> 1) & 1) ^ 1)) {
+        set_abort(S, args.err, kErrTimeoutProducer);
+        break;
+      }
+      float* buf = S.tile_buf[tb];
+      if constexpr (MODE == 1) {
+        // 14 chunks of 16 B per 56-float row: lanes 0-13 gate row, 14-27 up row
+        if (lane < 28) {
+          const int row = lane < 14 ? nt : 16 + nt, c = lane < 14 ? lane : lane - 14;
+          cp_async16(smem_u32(buf + (lane < 14 ? 0 : 64) + 4 * c),
+                     args.sb + ((size_t)e * 32 + row) * kHiddenBlocks + 4 * c);
+        }
+      } else {
+        // 8 chunks of weight scales, 16 of tokens, 16 of weights
+        const size_t p0 = (size_t)S.row_off[e] + mt * (BM / 2);     // the tile's first pair
+        for (int c = lane; c < 40; c += 32) {
+          if (c < 8) cp_async16(smem_u32(buf + 4 * c), args.sb + ((size_t)e * kHiddenBlocks + 2 * nt) * kInterBlocks + 4 * c);
+          else if (c < 24) cp_async16(smem_u32(buf + 64 + 4 * (c - 8)), args.row_token + p0 + 4 * (c - 8));
+          else cp_async16(smem_u32(buf + 128 + 4 * (c - 24)), args.row_weight + p0 + 4 * (c - 24));
+        }
+      }
+      cp_async_mbar_arrive(smem_u32(&S.tbfull[tb]));
+      for (int kb = 0; kb < KB; ++kb, ++kq) {
+        const int ss = kq % kScaleRing, su = kq / kScaleRing;
+        if (!mbar_wait(smem_u32(&S.scempty[ss]), (su & 1) ^ 1)) {
+          set_abort(S, args.err, kErrTimeoutProducer);
+          ok = false;
+          break;
+        }
+        cp_async16(smem_u32(&S.sa_ring[ss][4 * lane]), args.sa + (size_t)kb * ld_sa + arow + 4 * lane);
+        cp_async_mbar_arrive(smem_u32(&S.scfull[ss]));
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp == STORE_WARP) {
+    // ------------------------------------------------------------ GEMM2 output reductions
+    // For every tile, take each epilogue warp's 16 staged rows and add them to
+    // the fp32 token accumulator with asynchronous bulk reductions (lanes 0-15,
+    // one 512-byte row each), so the epilogue never waits on the memory system.
+    if constexpr (MODE == 2) {
+      int j = 0;
+      for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++j) {
+        int e, nt, mt;
+        decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
+        bool ok = true;
+        for (int w = 0; w < EPI_WARPS && ok; ++w) {
+          if (!mbar_wait(smem_u32(&S.staged[w]), j & 1)) {
+            set_abort(S, args.err, kErrTimeoutEpilogue);
+            ok = false;
+            break;
+          }
+          const int tok = lane < 16 ? S.row_tok[w][lane] : -1;
+          if (tok >= 0) {
+            const uint8_t* row = staging + (size_t)(w * 16 + lane) * Cfg::ROW_STRIDE;
+            float* dst = args.out_acc + (size_t)tok * kHidden + nt * BN + 128 * (w >> 2);
+            bulk_reduce_add_f32(dst, smem_u32(row), 128 * sizeof(float));
+            bulk_commit();
+          }
+          bulk_wait_read_all();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&S.sfree[w]));
+        }
+        if (!ok) break;
+      }
+      bulk_wait_all();                   // reductions complete before the CTA exits
+    }
   } else {
     // ------------------------------------------------------------ promotion + epilogue
     const int ew = warp - 2;
@@ -285,72 +422,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int g = ew >> 2;           // column half
     const int r = 32 * q + lane;     // row inside the tile
     const uint32_t lane_addr = tmem_base + ((uint32_t)(32 * q) << 16);
-    // Per-tile epilogue state. The next tile's state (its block-scale pointers
-    // and first kScalePrefetch scales) is loaded before the current tile's
-    // output work, so those global-load latencies overlap that work.
-    constexpr int PF = kScalePrefetch;
-    static_assert(KB % PF == 0, "K-blocks must be a multiple of the prefetch depth");
-    struct TileState {
-      int e, nt, row_in_expert, arow;
-      bool valid;
-      const float* sbp;
-      const float* sbp2;
-      float sa_r[PF], sb_r[PF], sb2_r[PF];
-    };
-    const size_t ld_sa = (size_t)Cfg::ROWS_PER_PAIR * args.R1;
-    auto load_state = [&](int t, TileState& ts) {
-      int mt;
-      decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, ts.e, ts.nt, mt);
-      ts.row_in_expert = mt * BM + r;                         // GEMM row inside the expert's group
-      ts.arow = Cfg::ROWS_PER_PAIR * S.row_off[ts.e] + ts.row_in_expert;
-      ts.valid = ts.row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[ts.e];
-      if (MODE == 1) {
-        ts.sbp = args.sb + ((size_t)ts.e * 32 + ts.nt) * kHiddenBlocks;        // gate block row
-        ts.sbp2 = args.sb + ((size_t)ts.e * 32 + 16 + ts.nt) * kHiddenBlocks;  // up block row
-      } else {
-        ts.sbp = args.sb + ((size_t)ts.e * kHiddenBlocks + 2 * ts.nt + g) * kInterBlocks;
-        ts.sbp2 = nullptr;
-      }
-#pragma unroll
-      for (int u = 0; u < PF; ++u) {
-        ts.sa_r[u] = __ldg(args.sa + (size_t)u * ld_sa + ts.arow);
-        ts.sb_r[u] = __ldg(ts.sbp + u);
-        ts.sb2_r[u] = MODE == 1 ? __ldg(ts.sbp2 + u) : 0.f;
-      }
-    };
-    TileState cur, nxt;
-    if (blockIdx.x < total) load_state(blockIdx.x, nxt);
     int kt = 0, tile_iter = 0;
     for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++tile_iter) {
-      cur = nxt;
-      const int e = cur.e, nt = cur.nt, row_in_expert = cur.row_in_expert, arow = cur.arow;
-      const bool valid = cur.valid;
-      const float* sbp = cur.sbp;
-      const float* sbp2 = cur.sbp2;
+      int e, nt, mt;
+      decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
+      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
+      const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
+      const int tb = tile_iter & 1;
+      const float* tbuf = S.tile_buf[tb];
+      if (!mbar_wait(smem_u32(&S.tbfull[tb]), (tile_iter >> 1) & 1)) {
+        set_abort(S, args.err, kErrTimeoutEpilogue);
+        break;
+      }
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
-      // Block scales are prefetched kScalePrefetch K-blocks ahead in a register
-      // ring, so no global-load latency sits on the per-K-block critical path.
-      float sa_r[PF], sb_r[PF], sb2_r[PF];
-#pragma unroll
-      for (int u = 0; u < PF; ++u) {
-        sa_r[u] = cur.sa_r[u];
-        sb_r[u] = cur.sb_r[u];
-        sb2_r[u] = cur.sb2_r[u];
-      }
       bool ok = true;
-      for (int kb0 = 0; kb0 < KB && ok; kb0 += PF) {
-#pragma unroll
-        for (int u = 0; u < PF; ++u) {
-          const int kb = kb0 + u;
-          const float f0 = sa_r[u] * sb_r[u];
-          const float f1 = MODE == 1 ? sa_r[u] * sb2_r[u] : f0;
-          if (kb + PF < KB) {
-            sa_r[u] = __ldg(args.sa + (size_t)(kb + PF) * ld_sa + arow);
-            sb_r[u] = __ldg(sbp + kb + PF);
-            if (MODE == 1) sb2_r[u] = __ldg(sbp2 + kb + PF);
-          }
+      for (int kb = 0; kb < KB; ++kb) {
+        {
           const int b = kt & 1, v = kt >> 1;
           if (warp == 4 && lane == 0) trace_mark(kt, 0);
           if (!mbar_wait(smem_u32(&S.tfull[b]), v & 1)) {
@@ -358,8 +447,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             ok = false;
             break;
           }
+          const int ss = kt % kScaleRing;
+          if (!mbar_wait(smem_u32(&S.scfull[ss]), (kt / kScaleRing) & 1)) {
+            set_abort(S, args.err, kErrTimeoutEpilogue);
+            ok = false;
+            break;
+          }
           tc_fence_after();
           if (warp == 4 && lane == 0) trace_mark(kt, 1);
+          const float sa = S.sa_ring[ss][r];
+          const float f0 = sa * (MODE == 1 ? tbuf[kb] : tbuf[16 * g + kb]);
+          const float f1 = MODE == 1 ? sa * tbuf[64 + kb] : f0;
           const uint32_t base = lane_addr + (uint32_t)(b * BN);
 #pragma unroll
           for (int c = 0; c < 8; c += 2) {
@@ -378,16 +476,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&S.tempty[b]));
+          if (lane == 0) {
+            mbar_arrive(smem_u32(&S.tempty[b]));
+            mbar_arrive(smem_u32(&S.scempty[ss]));
+          }
           if (warp == 4 && lane == 0) trace_mark(kt, 2);
           ++kt;
         }
       }
       if (!ok) break;
       if (warp == 4 && lane == 0) trace_mark(kt - 1, 6);
-      if (t + (int)gridDim.x < total) load_state(t + gridDim.x, nxt);
 
-      if (MODE == 1) {
+      if constexpr (MODE == 1) {
         // SwiGLU: C = silu(X2) * X1 with X1 = gate half (cols < I), X2 = up half
         float amax = 0.f;
         if (valid) {                     // rows past the expert's count hold no data
@@ -443,17 +543,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       } else {
-        // combine: (hi row + lo row) * routing weight -> fp32 token accumulator
+        // combine: (hi row + lo row) * routing weight. Lanes 2p and 2p+1 hold
+        // the two 64-column halves of pair p's 128-column output row; the warp
+        // stages its 16 rows in shared memory for the store warp
         const int odd = lane & 1;
-        const int pair = row_in_expert >> 1;
-        const size_t prow = (size_t)S.row_off[e] + pair;
-        int token = 0;
-        float w = 0.f;
-        if (valid) {
-          token = __ldg(args.row_token + prow);
-          w = __ldg(args.row_weight + prow);
+        const float w = tbuf[128 + (r >> 1)];
+        const int token = reinterpret_cast<const int*>(tbuf)[64 + (r >> 1)];
+        uint8_t* wstage = staging + (size_t)ew * 16 * Cfg::ROW_STRIDE;
+        float* hrow = reinterpret_cast<float*>(wstage + (size_t)(lane >> 1) * Cfg::ROW_STRIDE + odd * 256);
+        if (!mbar_wait(smem_u32(&S.sfree[ew]), (tile_iter & 1) ^ 1)) {   // previous tile's rows read
+          set_abort(S, args.err, kErrTimeoutEpilogue);
+          break;
         }
-        float* dst = args.out_acc + (size_t)token * kHidden + nt * BN + 128 * g + (odd ? 64 : 0);
+        if (warp == 4 && lane == 0) trace_mark(kt - 1, 9);
 #pragma unroll
         for (int j4 = 0; j4 < 16; ++j4) {
           float o[4];
@@ -466,9 +568,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const float mine = odd ? bb : a;
             o[i] = (mine + recv) * w;
           }
-          if (valid) atomicAdd(reinterpret_cast<float4*>(dst) + j4, make_float4(o[0], o[1], o[2], o[3]));
+          reinterpret_cast<float4*>(hrow)[j4] = make_float4(o[0], o[1], o[2], o[3]);
         }
+        if (!odd) S.row_tok[ew][lane >> 1] = valid ? token : -1;
+        if (warp == 4 && lane == 0) trace_mark(kt - 1, 10);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&S.staged[ew]));
+        if (warp == 4 && lane == 0) trace_mark(kt - 1, 11);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&S.tbempty[tb]));   // this tile's scale buffer is free
       if (warp == 4 && lane == 0) trace_mark(kt - 1, 7);
     }
   }
@@ -490,11 +600,11 @@ cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
   cudaGetDevice(&dev);
   if (dev >= 64 || !g_smem_set[MODE - 1][dev]) {
     cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)GEMM_SMEM_BYTES);
+                                         (int)gemm_smem_bytes<MODE>());
     if (e != cudaSuccess) return e;
     if (dev < 64) g_smem_set[MODE - 1][dev] = 1;
   }
-  return launch_kernel(grouped_gemm_kernel<MODE>, dim3(num_sms), dim3(GEMM_THREADS), GEMM_SMEM_BYTES, st, true, tmA,
+  return launch_kernel(grouped_gemm_kernel<MODE>, dim3(num_sms), dim3(GEMM_THREADS), gemm_smem_bytes<MODE>(), st, true, tmA,
                        tmB, args);
 }
 

@@ -225,8 +225,8 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
   p.path = gemm_path(T);
   const bool s1 = p.path != 0, s2 = p.path >= 2;
   const uint32_t w2_box = s2 ? 128 : 256;
-  // streaming kernels: 128-byte boxes, 128-byte swizzle; tile kernels: 64-byte boxes, 64-byte swizzle
-  const uint32_t c1 = s1 ? 128 : 64, c2 = s2 ? 128 : 64;
+  // streaming kernels: 128-byte boxes, 128-byte swizzle; tile kernels: boxes as wide as their stages
+  const uint32_t c1 = s1 ? 128 : moe::kTileStageK1, c2 = s2 ? 128 : moe::kTileStageK2;
   if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, s1 ? 16 : 128, c1) ||
       !encode_fp8_2d(&p.tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128, c1) ||
       !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, s2 ? 16 : 128, c2) ||

@@ -25,6 +25,11 @@ constexpr int kTopKGroups = 4;
 constexpr int kBlock = 128;             // quantisation block edge
 constexpr int kHiddenBlocks = kHidden / kBlock;   // 56
 constexpr int kInterBlocks = kInter / kBlock;     // 16
+// K width of one shared-memory stage of the 128-row tile GEMMs (128: 128-byte
+// swizzle, one stage per scale block; 64: 64-byte swizzle, two stages per
+// block). The tensor maps of those GEMMs are built with the same box width.
+constexpr int kTileStageK1 = 128;   // GEMM1
+constexpr int kTileStageK2 = 128;   // GEMM2
 constexpr float kFp8Max = 448.f;
 constexpr int kMaxLocalExperts = 256;
 
@@ -110,6 +115,37 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
                : "memory");
 }
+
+// 1-D bulk reduction shared -> global: dst[i] += src[i] over `bytes` of fp32
+// (16-byte aligned addresses, size a multiple of 16), tracked by the issuing
+// thread's bulk async-group. The generic-proxy writes of src must be made
+// visible to the async proxy first (fence_proxy_async_smem).
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until this thread's bulk groups have finished reading their shared-memory sources.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until this thread's bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (both addresses 16-byte aligned).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src))
+               : "memory");
+}
+// The mbarrier receives one arrival once all of this thread's earlier cp.async
+// copies have completed (the arrival is part of the barrier's initial count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // ------------------------------------------------------------------ tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
