@@ -71,6 +71,7 @@ struct GemmSmem {
   // GEMM2: [0,32) scales of output column blocks 2nt and 2nt+1, [64,128) the
   // tile's 64 pair tokens (int), [128,192) their routing weights.
   alignas(16) float tile_buf[2][192];
+  int tile_info[2][4];          // the tile's expert, n-tile, m-tile, first pair row
   uint32_t tmem_base;
   int abort_flag;
   int total_tiles;
@@ -103,8 +104,10 @@ struct GemmCfg<1> {
   static constexpr int NT = kInter / 128;    // 16 n-tiles: 128 gate + 128 up columns each
   static constexpr int ROWS_PER_PAIR = 1;
   static constexpr int SK = kTileStageK1;
-  static constexpr int STAGES = SK == 128 ? 4 : 8;
-  static constexpr int STAGING = 0;
+  static constexpr int STAGES = SK == 128 ? 3 : 8;
+  // per epilogue warp: its 32 rows' hi and lo 64-byte pieces, two 2 KB boxes
+  // in the 64-byte swizzle layout of the output tensor map
+  static constexpr int STAGING = EPI_WARPS * 4096;
 };
 template <>
 struct GemmCfg<2> {
@@ -193,7 +196,7 @@ __device__ __forceinline__ float2 unpack_e4m3x2(uint32_t v16) {
 template <int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmOut, GemmArgs args) {
   using Cfg = GemmCfg<MODE>;
   constexpr int KB = Cfg::KB, NT = Cfg::NT, STAGES = Cfg::STAGES, SK = Cfg::SK, HS = BK / SK;
   constexpr int A_TILE = BM * SK, B_TILE = BN * SK, STAGE_BYTES = A_TILE + B_TILE;
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(smem_u32(&S.scempty[i]), EPI_WARPS);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&S.tbfull[b]), 32);
+      mbar_init(smem_u32(&S.tbfull[b]), 33);     // 32 cp.async arrivals + the tile info
       mbar_init(smem_u32(&S.tbempty[b]), EPI_WARPS);
     }
     S.abort_flag = 0;
@@ -371,6 +374,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
       cp_async_mbar_arrive(smem_u32(&S.tbfull[tb]));
+      if (lane == 0) {
+        S.tile_info[tb][0] = e;
+        S.tile_info[tb][1] = nt;
+        S.tile_info[tb][2] = mt;
+        S.tile_info[tb][3] = S.row_off[e];
+        mbar_arrive(smem_u32(&S.tbfull[tb]));
+      }
       for (int kb = 0; kb < KB; ++kb, ++kq) {
         const int ss = kq % kScaleRing, su = kq / kScaleRing;
         if (!mbar_wait(smem_u32(&S.scempty[ss]), (su & 1) ^ 1)) {
@@ -424,16 +434,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t lane_addr = tmem_base + ((uint32_t)(32 * q) << 16);
     int kt = 0, tile_iter = 0;
     for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++tile_iter) {
-      int e, nt, mt;
-      decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
-      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
-      const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
+      // the scale loader publishes the decoded tile with the tile's scales
       const int tb = tile_iter & 1;
       const float* tbuf = S.tile_buf[tb];
+      if (warp == 4 && lane == 0) trace_mark(kt, 12);
       if (!mbar_wait(smem_u32(&S.tbfull[tb]), (tile_iter >> 1) & 1)) {
         set_abort(S, args.err, kErrTimeoutEpilogue);
         break;
       }
+      const int e = S.tile_info[tb][0], nt = S.tile_info[tb][1], mt = S.tile_info[tb][2];
+      const int row_off_e = S.tile_info[tb][3];
+      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
+      const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
+      if (warp == 4 && lane == 0) trace_mark(kt, 13);
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
@@ -486,6 +499,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       if (!ok) break;
       if (warp == 4 && lane == 0) trace_mark(kt - 1, 6);
+      // GEMM2's pair token and weight are the last reads of this tile's scale
+      // buffer; release it before the output work (whose global stores the
+      // release would otherwise wait for)
+      const float w_pair = MODE == 2 ? tbuf[128 + (r >> 1)] : 0.f;
+      const int tok_pair = MODE == 2 ? reinterpret_cast<const int*>(tbuf)[64 + (r >> 1)] : 0;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&S.tbempty[tb]));
 
       if constexpr (MODE == 1) {
         // SwiGLU: C = silu(X2) * X1 with X1 = gate half (cols < I), X2 = up half
@@ -510,45 +530,60 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         amax = fmaxf(amax, S.amax_x[xb][g ^ 1][r]);
         if (warp == 4 && lane == 0) trace_mark(kt - 1, 9);
-        if (valid) {
-          const float s_hi = amax / kFp8Max;
-          const float inv_hi = amax > 0.f ? kFp8Max / amax : 0.f;
-          const float s_lo = s_hi * (1.0f / 16.0f);
-          const float inv_lo = inv_hi * 16.0f;
-          uint32_t hi[16], lo[16];
+        // two-term quantisation, staged in the store boxes' 64-byte swizzle
+        // (16-byte chunk c of row l sits at chunk c ^ ((l >> 1) & 3)), then
+        // written by two TMA tensor stores per warp (rows past the expert's
+        // count fill padding rows whose GEMM2 outputs are discarded)
+        uint8_t* box_hi = staging + (size_t)ew * 4096;
+        uint8_t* box_lo = box_hi + 2048;
+        if (lane == 0) bulk_wait_read_all();                  // previous tile's boxes have been read
+        __syncwarp();
+        const float s_hi = amax / kFp8Max;
+        const float inv_hi = amax > 0.f ? kFp8Max / amax : 0.f;
+        const float s_lo = s_hi * (1.0f / 16.0f);
+        const float inv_lo = inv_hi * 16.0f;
+        const int sw = (lane >> 1) & 3;
 #pragma unroll
-          for (int j4 = 0; j4 < 16; ++j4) {
+        for (int k = 0; k < 4; ++k) {
+          uint32_t hi[4], lo[4];
+#pragma unroll
+          for (int m4 = 0; m4 < 4; ++m4) {
+            const int j4 = 4 * k + m4;
             float c[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) c[i] = acc[4 * j4 + i];
-            hi[j4] = pack_e4m3x4(c[0] * inv_hi, c[1] * inv_hi, c[2] * inv_hi, c[3] * inv_hi);
-            const float2 h01 = unpack_e4m3x2(hi[j4] & 0xffffu);
-            const float2 h23 = unpack_e4m3x2(hi[j4] >> 16);
-            lo[j4] = pack_e4m3x4((c[0] - h01.x * s_hi) * inv_lo, (c[1] - h01.y * s_hi) * inv_lo,
+            hi[m4] = pack_e4m3x4(c[0] * inv_hi, c[1] * inv_hi, c[2] * inv_hi, c[3] * inv_hi);
+            const float2 h01 = unpack_e4m3x2(hi[m4] & 0xffffu);
+            const float2 h23 = unpack_e4m3x2(hi[m4] >> 16);
+            lo[m4] = pack_e4m3x4((c[0] - h01.x * s_hi) * inv_lo, (c[1] - h01.y * s_hi) * inv_lo,
                                  (c[2] - h23.x * s_hi) * inv_lo, (c[3] - h23.y * s_hi) * inv_lo);
           }
-          const size_t prow = (size_t)S.row_off[e] + row_in_expert;  // pair row
-          uint8_t* dhi = args.a2 + (2 * prow) * kInter + nt * 128 + 64 * g;
-          uint8_t* dlo = dhi + kInter;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            reinterpret_cast<uint4*>(dhi)[k] = make_uint4(hi[4 * k], hi[4 * k + 1], hi[4 * k + 2], hi[4 * k + 3]);
-            reinterpret_cast<uint4*>(dlo)[k] = make_uint4(lo[4 * k], lo[4 * k + 1], lo[4 * k + 2], lo[4 * k + 3]);
-          }
-          if (warp == 4 && lane == 0) trace_mark(kt - 1, 10);
-          if (g == 0) {
-            float* sa2 = args.sa2 + (size_t)nt * 2 * args.R1 + 2 * prow;
-            sa2[0] = s_hi;
-            sa2[1] = s_lo;
-          }
+          const int off = lane * 64 + ((k ^ sw) << 4);
+          *reinterpret_cast<uint4*>(box_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(box_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int y = row_off_e + mt * BM + 32 * q;         // pair row of the warp's first row
+          tma_store_2d(&tmOut, smem_u32(box_hi), nt * 128 + 64 * g, y);
+          tma_store_2d(&tmOut, smem_u32(box_lo), kInter + nt * 128 + 64 * g, y);
+          bulk_commit();
+        }
+        if (warp == 4 && lane == 0) trace_mark(kt - 1, 10);
+        if (valid && g == 0) {
+          const size_t prow = (size_t)row_off_e + row_in_expert;  // pair row
+          float* sa2 = args.sa2 + (size_t)nt * 2 * args.R1 + 2 * prow;
+          sa2[0] = s_hi;
+          sa2[1] = s_lo;
         }
       } else {
         // combine: (hi row + lo row) * routing weight. Lanes 2p and 2p+1 hold
         // the two 64-column halves of pair p's 128-column output row; the warp
         // stages its 16 rows in shared memory for the store warp
         const int odd = lane & 1;
-        const float w = tbuf[128 + (r >> 1)];
-        const int token = reinterpret_cast<const int*>(tbuf)[64 + (r >> 1)];
+        const float w = w_pair;
+        const int token = tok_pair;
         uint8_t* wstage = staging + (size_t)ew * 16 * Cfg::ROW_STRIDE;
         float* hrow = reinterpret_cast<float*>(wstage + (size_t)(lane >> 1) * Cfg::ROW_STRIDE + odd * 256);
         if (!mbar_wait(smem_u32(&S.sfree[ew]), (tile_iter & 1) ^ 1)) {   // previous tile's rows read
@@ -577,12 +612,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (lane == 0) mbar_arrive(smem_u32(&S.staged[ew]));
         if (warp == 4 && lane == 0) trace_mark(kt - 1, 11);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&S.tbempty[tb]));   // this tile's scale buffer is free
       if (warp == 4 && lane == 0) trace_mark(kt - 1, 7);
     }
   }
 
+  if (MODE == 1 && warp >= 2 && warp < 2 + EPI_WARPS && lane == 0) bulk_wait_all();   // output tiles written
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -594,8 +628,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 static int g_smem_set[2][64];
 
 template <int MODE>
-cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
-                          cudaStream_t st) {
+cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
+                          const GemmArgs& args, int num_sms, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !g_smem_set[MODE - 1][dev]) {
@@ -605,7 +639,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
     if (dev < 64) g_smem_set[MODE - 1][dev] = 1;
   }
   return launch_kernel(grouped_gemm_kernel<MODE>, dim3(num_sms), dim3(GEMM_THREADS), gemm_smem_bytes<MODE>(), st, true, tmA,
-                       tmB, args);
+                       tmB, tmOut, args);
 }
 
 cudaError_t set_trace(int on) {
@@ -621,13 +655,13 @@ cudaError_t read_trace(unsigned long long* host, int n) {
   return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * n);
 }
 
-cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
-                         cudaStream_t st) {
-  return launch_gemm_t<1>(tmA, tmB, args, num_sms, st);
+cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
+                         const GemmArgs& args, int num_sms, cudaStream_t st) {
+  return launch_gemm_t<1>(tmA, tmB, tmOut, args, num_sms, st);
 }
 cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
                          cudaStream_t st) {
-  return launch_gemm_t<2>(tmA, tmB, args, num_sms, st);
+  return launch_gemm_t<2>(tmA, tmB, tmA, args, num_sms, st);   // GEMM2 stores no tiles
 }
 
 }  // namespace moe

@@ -166,7 +166,7 @@ struct Plan {
   int nsm;
   int* counts; int* topk_idx; float* topk_w; int* pair_pos; int* row_token; float* row_weight;
   uint8_t* a1; float* sa1; uint8_t* a2; float* sa2; float* acc; int* err;
-  CUtensorMap tmA1, tmB1, tmA2, tmB2;
+  CUtensorMap tmA1, tmB1, tmA2, tmB2, tmO1;
   int path;  // see gemm_path()
 };
 
@@ -230,7 +230,8 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
   if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, s1 ? 16 : 128, c1) ||
       !encode_fp8_2d(&p.tmB1, a->gemm1_weights, moe::kHidden, (uint64_t)E * moe::kGemm1N, 128, c1) ||
       !encode_fp8_2d(&p.tmA2, p.a2, moe::kInter, 2ull * L.R1, s2 ? 16 : 128, c2) ||
-      !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, w2_box, c2))
+      !encode_fp8_2d(&p.tmB2, a->gemm2_weights, moe::kInter, (uint64_t)E * moe::kHidden, w2_box, c2) ||
+      !encode_fp8_2d(&p.tmO1, p.a2, 2 * moe::kInter, L.R1, 32, 64))
     return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   return MOE_OK;
 }
@@ -309,7 +310,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
         g.sb = a->gemm1_weights_scale;
         g.a2 = p.a2;
         g.sa2 = p.sa2;
-        e = moe::launch_gemm1(p.tmA1, p.tmB1, g, p.nsm, st);
+        e = moe::launch_gemm1(p.tmA1, p.tmB1, p.tmO1, g, p.nsm, st);
       } else {
         g.sa = p.sa2;
         g.sb = a->gemm2_weights_scale;

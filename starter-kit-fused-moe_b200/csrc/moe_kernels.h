@@ -61,8 +61,10 @@ cudaError_t launch_quantize(const void* x, bool bf16, int T, uint8_t* q, float* 
 void set_last_error(const char* msg);
 cudaError_t set_trace(int on);
 cudaError_t read_trace(unsigned long long* host, int n);
-cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
-                         cudaStream_t st);
+// tmOut: the GEMM2 operand viewed as [R1, 4096] bytes (hi row | lo row of
+// each pair), 32 x 64-byte boxes, 64-byte swizzle; GEMM1 stores its output tiles through it.
+cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
+                         const GemmArgs& args, int num_sms, cudaStream_t st);
 cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
                          cudaStream_t st);
 
