@@ -38,6 +38,7 @@
 //          tile's main loop.
 #include "moe_common.cuh"
 #include "moe_kernels.h"
+#include "moe_workspace.h"
 
 namespace moe {
 
@@ -52,6 +53,7 @@ constexpr int SCALE_WARP = 11;
 constexpr int EPI_WARPS = 8;
 constexpr int TMEM_COLS = 512;
 constexpr int kScaleRing = 8;        // K-blocks of activation scales in flight
+constexpr int kEpiBarrier = 1;       // named barrier of the 8 epilogue warps
 
 struct GemmSmem {
   uint64_t full[MAX_STAGES];
@@ -71,7 +73,10 @@ struct GemmSmem {
   // GEMM2: [0,32) scales of output column blocks 2nt and 2nt+1, [64,128) the
   // tile's 64 pair tokens (int), [128,192) their routing weights.
   alignas(16) float tile_buf[2][192];
-  int tile_info[2][4];          // the tile's expert, n-tile, m-tile, first pair row
+  int tile_info[2][8];          // the unit's expert, n-tile, m-tile, first pair row, K-blocks [k0, k1),
+                                // split slot (-1: whole tile), split tail-tile index
+  int units, full_tiles, splits;  // work units: whole tiles, then `splits` K-slices per tail tile
+  int split_last[2];            // GEMM1: this CTA completed the split tile
   uint32_t tmem_base;
   int abort_flag;
   int total_tiles;
@@ -92,8 +97,12 @@ constexpr int kTraceKBlocks = 512, kTraceSlots = 16;
 __device__ unsigned long long g_trace[kTraceKBlocks * kTraceSlots];
 __device__ int g_trace_on;
 
+// The marks are compiled in only with -DMOE_GEMM_TRACE (they cost registers
+// in the epilogue's main loop); otherwise the timeline stays zero.
 __device__ __forceinline__ void trace_mark(int kt, int slot) {
+#ifdef MOE_GEMM_TRACE
   if (blockIdx.x == 0 && kt < kTraceKBlocks && g_trace_on) g_trace[kt * kTraceSlots + slot] = clock64();
+#endif
 }
 
 template <int MODE>
@@ -104,6 +113,7 @@ struct GemmCfg<1> {
   static constexpr int NT = kInter / 128;    // 16 n-tiles: 128 gate + 128 up columns each
   static constexpr int ROWS_PER_PAIR = 1;
   static constexpr int SK = kTileStageK1;
+  static constexpr int MAX_SPLITS = 6;         // each extra slice costs one partial-tile read in the fix-up
   static constexpr int STAGES = SK == 128 ? 3 : 8;
   // per epilogue warp: its 32 rows' hi and lo 64-byte pieces, two 2 KB boxes
   // in the 64-byte swizzle layout of the output tensor map
@@ -115,6 +125,7 @@ struct GemmCfg<2> {
   static constexpr int NT = kHidden / BN;    // 28 n-tiles of 256 output columns
   static constexpr int ROWS_PER_PAIR = 2;    // hi and lo term rows
   static constexpr int SK = kTileStageK2;
+  static constexpr int MAX_SPLITS = 4;         // slices of at least 4 K-blocks
   static constexpr int STAGES = SK == 128 ? 3 : 6;
   // per epilogue warp: 16 output rows of 128 fp32 (512 B), 528 B apart so the
   // float4 writes of 8 consecutive lanes fall in at most 2-way bank conflicts
@@ -173,6 +184,35 @@ __device__ __forceinline__ void decode_tile(const GemmSmem& S, int E, int rows_p
   const int m = (S.cnt[e] * rows_per_pair + BM - 1) / BM;
   nt = local / m;
   mt = local - nt * m;
+}
+
+// Work units. The tile list is walked round-robin by the persistent CTAs; when
+// the last round would be partial (tail = tiles % grid), each tail tile is cut
+// into `splits` K-slices so the tail spreads over the whole grid. GEMM2's
+// slices simply add their partial outputs; GEMM1's slices meet in a fix-up
+// (the last slice to arrive sums the others' fp32 partials and runs the
+// epilogue).
+struct Unit {
+  int tile, k0, k1, slot, tail;   // slot: split index among all split units, -1 for a whole tile
+};
+__device__ __forceinline__ Unit unit_of(const GemmSmem& S, int u, int KB) {
+  Unit x;
+  if (u < S.full_tiles) {
+    x.tile = u;
+    x.k0 = 0;
+    x.k1 = KB;
+    x.slot = -1;
+    x.tail = -1;
+  } else {
+    const int v = u - S.full_tiles, sp = S.splits;
+    const int i = v / sp, j = v - i * sp;
+    x.tile = S.full_tiles + i;
+    x.k0 = j * KB / sp;
+    x.k1 = (j + 1) * KB / sp;
+    x.slot = v;
+    x.tail = i;
+  }
+  return x;
 }
 
 __device__ __forceinline__ void set_abort(GemmSmem& S, int* err, int code) {
@@ -254,6 +294,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (tid == 0) {
       S.tile_start[E] = tot1;
       S.total_tiles = tot1;
+      const int G = gridDim.x;
+      int tail = tot1 % G, sp = 1;
+      if (tail > 0) {
+        sp = min(min(G / tail, Cfg::MAX_SPLITS), (int)(WsLayout::kMaxSplitUnits / tail));
+        if (sp < 2) sp = 1;
+      }
+      if (sp == 1) tail = 0;
+      S.splits = sp;
+      S.full_tiles = tot1 - tail;
+      S.units = tot1 - tail + tail * sp;
     }
   }
   if (warp == 1) {
@@ -264,18 +314,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = S.tmem_base;
-  const int total = S.total_tiles;
+  const int units = S.units;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
+      for (int u = blockIdx.x; u < units && ok && !aborted(S); u += gridDim.x) {
+        const Unit x = unit_of(S, u, KB);
         int e, nt, mt;
-        decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
+        decode_tile(S, E, Cfg::ROWS_PER_PAIR, x.tile, e, nt, mt);
         const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
-        for (int ks = 0; ks < KB * HS; ++ks, ++it) {
+        for (int ks = x.k0 * HS; ks < x.k1 * HS; ++ks, ++it) {
           const int s = it % STAGES, u = it / STAGES;
           if (!mbar_wait(smem_u32(&S.empty[s]), (u & 1) ^ 1)) {
             set_abort(S, args.err, kErrTimeoutProducer);
@@ -304,8 +355,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
       int it = 0, kt = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x) {
-        for (int kb = 0; kb < KB && ok; ++kb, ++kt) {
+      for (int u = blockIdx.x; u < units && ok && !aborted(S); u += gridDim.x) {
+        const Unit x = unit_of(S, u, KB);
+        for (int kb = x.k0; kb < x.k1 && ok; ++kb, ++kt) {
           const int b = kt & 1, v = kt >> 1;
           trace_mark(kt, 3);
           if (!mbar_wait(smem_u32(&S.tempty[b]), (v & 1) ^ 1)) {
@@ -347,9 +399,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const size_t ld_sa = (size_t)Cfg::ROWS_PER_PAIR * args.R1;
     int kq = 0, j = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok && !aborted(S); t += gridDim.x, ++j) {
+    for (int u = blockIdx.x; u < units && ok && !aborted(S); u += gridDim.x, ++j) {
+      const Unit x = unit_of(S, u, KB);
       int e, nt, mt;
-      decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
+      decode_tile(S, E, Cfg::ROWS_PER_PAIR, x.tile, e, nt, mt);
       const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
       const int tb = j & 1;
       if (!mbar_wait(smem_u32(&S.tbempty[tb]), ((j >> 1) & 1) ^ 1)) {
@@ -379,9 +432,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         S.tile_info[tb][1] = nt;
         S.tile_info[tb][2] = mt;
         S.tile_info[tb][3] = S.row_off[e];
+        S.tile_info[tb][4] = x.k0;
+        S.tile_info[tb][5] = x.k1;
+        S.tile_info[tb][6] = x.slot;
+        S.tile_info[tb][7] = x.tail;
         mbar_arrive(smem_u32(&S.tbfull[tb]));
       }
-      for (int kb = 0; kb < KB; ++kb, ++kq) {
+      for (int kb = x.k0; kb < x.k1; ++kb, ++kq) {
         const int ss = kq % kScaleRing, su = kq / kScaleRing;
         if (!mbar_wait(smem_u32(&S.scempty[ss]), (su & 1) ^ 1)) {
           set_abort(S, args.err, kErrTimeoutProducer);
@@ -400,9 +457,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // one 512-byte row each), so the epilogue never waits on the memory system.
     if constexpr (MODE == 2) {
       int j = 0;
-      for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++j) {
+      for (int u = blockIdx.x; u < units && !aborted(S); u += gridDim.x, ++j) {
+        const Unit x = unit_of(S, u, KB);
         int e, nt, mt;
-        decode_tile(S, E, Cfg::ROWS_PER_PAIR, t, e, nt, mt);
+        decode_tile(S, E, Cfg::ROWS_PER_PAIR, x.tile, e, nt, mt);
         bool ok = true;
         for (int w = 0; w < EPI_WARPS && ok; ++w) {
           if (!mbar_wait(smem_u32(&S.staged[w]), j & 1)) {
@@ -432,8 +490,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int g = ew >> 2;           // column half
     const int r = 32 * q + lane;     // row inside the tile
     const uint32_t lane_addr = tmem_base + ((uint32_t)(32 * q) << 16);
-    int kt = 0, tile_iter = 0;
-    for (int t = blockIdx.x; t < total && !aborted(S); t += gridDim.x, ++tile_iter) {
+    int kt = 0, tile_iter = 0, amax_iter = 0;
+    for (int u = blockIdx.x; u < units && !aborted(S); u += gridDim.x, ++tile_iter) {
       // the scale loader publishes the decoded tile with the tile's scales
       const int tb = tile_iter & 1;
       const float* tbuf = S.tile_buf[tb];
@@ -442,16 +500,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         set_abort(S, args.err, kErrTimeoutEpilogue);
         break;
       }
-      const int e = S.tile_info[tb][0], nt = S.tile_info[tb][1], mt = S.tile_info[tb][2];
-      const int row_off_e = S.tile_info[tb][3];
-      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
-      const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
+      // only the K range is live through the main loop; the rest of the tile's
+      // description is read after it (registers are the epilogue's limit)
+      const int k0 = S.tile_info[tb][4], k1 = S.tile_info[tb][5];
       if (warp == 4 && lane == 0) trace_mark(kt, 13);
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
+      for (int kb = k0; kb < k1; ++kb) {
         {
           const int b = kt & 1, v = kt >> 1;
           if (warp == 4 && lane == 0) trace_mark(kt, 0);
@@ -473,19 +530,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const float f1 = MODE == 1 ? sa * tbuf[64 + kb] : f0;
           const uint32_t base = lane_addr + (uint32_t)(b * BN);
 #pragma unroll
-          for (int c = 0; c < 8; c += 2) {
+          for (int c = 0; c < 8; ++c) {
             // MODE 1: chunks 0-3 = gate columns 64g.., chunks 4-7 = up columns 128+64g..
             const int col0 = MODE == 1 ? (c < 4 ? 64 * g + 16 * c : 128 + 64 * g + 16 * (c - 4)) : 128 * g + 16 * c;
-            float p0[16], p1[16];
+            float p0[16];
             tmem_ld16(base + col0, p0);
-            tmem_ld16(base + col0 + 16, p1);
             tmem_ld_wait();
             const float f = c < 4 ? f0 : f1;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              acc[16 * c + i] = fmaf(p0[i], f, acc[16 * c + i]);
-              acc[16 * c + 16 + i] = fmaf(p1[i], f, acc[16 * c + 16 + i]);
-            }
+            for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(p0[i], f, acc[16 * c + i]);
           }
           tc_fence_before();
           __syncwarp();
@@ -502,12 +555,46 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // GEMM2's pair token and weight are the last reads of this tile's scale
       // buffer; release it before the output work (whose global stores the
       // release would otherwise wait for)
+      const int e = S.tile_info[tb][0], nt = S.tile_info[tb][1], mt = S.tile_info[tb][2];
+      const int row_off_e = S.tile_info[tb][3];
+      const int slot = S.tile_info[tb][6], tail_i = S.tile_info[tb][7];
+      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
+      const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
       const float w_pair = MODE == 2 ? tbuf[128 + (r >> 1)] : 0.f;
       const int tok_pair = MODE == 2 ? reinterpret_cast<const int*>(tbuf)[64 + (r >> 1)] : 0;
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.tbempty[tb]));
 
       if constexpr (MODE == 1) {
+        if (slot >= 0) {
+          // K-split tail tile: publish this slice's fp32 partial; the slice
+          // that arrives last sums all of them and runs the epilogue.
+          const int sp = S.splits;
+          float4* part = reinterpret_cast<float4*>(args.split_partial);
+          const size_t base = (size_t)slot * (EPI_WARPS * 32 * 32) + (size_t)ew * 32 * 32 + lane;
+#pragma unroll
+          for (int j4 = 0; j4 < 32; ++j4)
+            __stcg(part + base + 32 * j4, make_float4(acc[4 * j4], acc[4 * j4 + 1], acc[4 * j4 + 2], acc[4 * j4 + 3]));
+          __threadfence();
+          named_barrier_sync(kEpiBarrier, EPI_WARPS * 32);
+          if (ew == 0 && lane == 0) S.split_last[tb] = atomicAdd(args.split_cnt + tail_i, 1) == sp - 1;
+          named_barrier_sync(kEpiBarrier, EPI_WARPS * 32);
+          if (!S.split_last[tb]) continue;
+          __threadfence();
+          const int first = slot - (slot % sp);
+          for (int o = first; o < first + sp; ++o) {
+            if (o == slot) continue;
+            const size_t ob = (size_t)o * (EPI_WARPS * 32 * 32) + (size_t)ew * 32 * 32 + lane;
+#pragma unroll
+            for (int j4 = 0; j4 < 32; ++j4) {
+              const float4 v = __ldcg(part + ob + 32 * j4);
+              acc[4 * j4] += v.x;
+              acc[4 * j4 + 1] += v.y;
+              acc[4 * j4 + 2] += v.z;
+              acc[4 * j4 + 3] += v.w;
+            }
+          }
+        }
         // SwiGLU: C = silu(X2) * X1 with X1 = gate half (cols < I), X2 = up half
         float amax = 0.f;
         if (valid) {                     // rows past the expert's count hold no data
@@ -520,15 +607,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (warp == 4 && lane == 0) trace_mark(kt - 1, 8);
         // exchange the row maximum with the warp that holds the other 64 columns
-        const int xb = tile_iter & 1;
+        const int xb = amax_iter & 1;
         S.amax_x[xb][g][r] = amax;
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&S.amax_bar[xb]));
-        if (!mbar_wait(smem_u32(&S.amax_bar[xb]), (tile_iter >> 1) & 1)) {
+        if (!mbar_wait(smem_u32(&S.amax_bar[xb]), (amax_iter >> 1) & 1)) {
           set_abort(S, args.err, kErrTimeoutEpilogue);
           break;
         }
         amax = fmaxf(amax, S.amax_x[xb][g ^ 1][r]);
+        ++amax_iter;
         if (warp == 4 && lane == 0) trace_mark(kt - 1, 9);
         // two-term quantisation, staged in the store boxes' 64-byte swizzle
         // (16-byte chunk c of row l sits at chunk c ^ ((l >> 1) & 3)), then

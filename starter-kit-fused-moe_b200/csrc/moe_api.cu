@@ -310,6 +310,8 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
         g.sb = a->gemm1_weights_scale;
         g.a2 = p.a2;
         g.sa2 = p.sa2;
+        g.split_partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a->workspace) + p.L.split_partial);
+        g.split_cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a->workspace) + p.L.split_cnt());
         e = moe::launch_gemm1(p.tmA1, p.tmB1, p.tmO1, g, p.nsm, st);
       } else {
         g.sa = p.sa2;

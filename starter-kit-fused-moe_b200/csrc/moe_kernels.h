@@ -18,6 +18,8 @@ struct GemmArgs {
   const int* row_token;    // GEMM2: token of each pair row
   const float* row_weight; // GEMM2: routing weight of each pair row
   float* out_acc;          // GEMM2 out: f32 [T, 7168]
+  float* split_partial;    // GEMM1: fp32 partial tiles of K-split tail tiles
+  int* split_cnt;          // GEMM1: arrivals per split tail tile (zero at launch)
   int* err;                // device error word
 };
 

@@ -16,7 +16,8 @@ struct WsLayout {
   int T, E, R1;               // tokens, local experts, pair-row capacity
   size_t err;                 // int32 error word (sticky; cleared by the host reader)
   size_t counts;              // int32 [E]   pairs per local expert, then the streaming kernel's
-                              //             tile queue [2] and per-expert GEMM1 progress [256]
+                              //             tile queue [2], per-expert GEMM1 progress [256] and
+                              //             the tile GEMM1's split-tile arrival counters [256]
   size_t topk_idx;            // int32 [T*8] selected global experts (selection order)
   size_t topk_w;              // f32   [T*8] combine weights
   size_t pair_pos;            // int32 [T*8] position inside the expert's group, -1 if not local
@@ -27,10 +28,13 @@ struct WsLayout {
   size_t a2;                  // e4m3  [2*R1, 2048] SwiGLU output, two FP8 terms per pair row
   size_t sa2;                 // f32   [16, 2*R1]   their 1x128 scales
   size_t out_acc;             // f32   [T, 7168]    combine accumulator
+  size_t split_partial;       // f32   [kMaxSplitUnits, 128*256] tile GEMM1 K-split partial tiles
   size_t total;
   size_t queue() const { return counts + sizeof(int32_t) * 256; }
   size_t done1() const { return counts + sizeof(int32_t) * 258; }
-  static constexpr size_t kCountersBytes = sizeof(int32_t) * (256 + 2 + 256);
+  size_t split_cnt() const { return counts + sizeof(int32_t) * 514; }
+  static constexpr size_t kCountersBytes = sizeof(int32_t) * (256 + 2 + 256 + 256);
+  static constexpr int kMaxSplitUnits = 160;
 };
 
 inline size_t ws_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -57,6 +61,7 @@ inline WsLayout ws_layout(int T, int E) {
   L.a2 = take((size_t)2 * L.R1 * 2048);
   L.sa2 = take(sizeof(float) * 16 * 2 * (size_t)L.R1);
   L.out_acc = take(sizeof(float) * 7168 * (size_t)T);
+  L.split_partial = take(sizeof(float) * 128 * 256 * (size_t)WsLayout::kMaxSplitUnits);
   L.total = o;
   return L;
 }

@@ -104,6 +104,42 @@ def test_many_tokens_per_expert(kernel_path, pkg, oracle, gpu_inputs):
     print(f"skewed T=600 {kernel_path}: max_abs_err={err:.3e}")
 
 
+def _tile_counts(oracle, x, E=32):
+    """Tiles of the two 128-row tile GEMMs for these inputs (GEMM1: 16 n-tiles per
+    128 pair rows of an expert; GEMM2: 28 n-tiles per 128 rows of hi/lo terms)."""
+    idx, _ = oracle.route(oracle.to_np(x.routing_logits), oracle.to_np(x.routing_bias), 2.5)
+    cnt = np.bincount(idx[idx < E].ravel(), minlength=E)
+    return int(sum(-(-c // 128) for c in cnt) * 16), int(sum(-(-(2 * c) // 128) for c in cnt) * 28)
+
+
+def test_tile_kernels_split_tail(pkg, oracle):
+    """A case whose last partial round of tiles is cut into K-slices in both tile
+    GEMMs (GEMM1 slices meet in the fix-up, GEMM2 slices add their partials);
+    two calls, so the slice arrival counters are reset between calls."""
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    found = None
+    for T in range(40, 1200, 7):      # routing draws come first: weights do not change it
+        t1, t2 = _tile_counts(oracle, pkg.inputs.make_inputs(T, seed=3, device="cuda", weight_experts=1))
+        if 0 < t1 % G <= G // 2 and 0 < t2 % G <= G // 2:
+            found = T
+            break
+    assert found is not None, "no token count with a split tail in both GEMMs"
+    T = found
+    x = pkg.inputs.make_inputs(T, seed=3, device="cuda", weight_experts=8)
+    old = pkg.set_gemm_path(0)
+    try:
+        outs = [pkg.run(*x.args()) for _ in range(2)]
+    finally:
+        pkg.set_gemm_path(old)
+    torch.cuda.synchronize()
+    assert pkg.read_device_error() == 0
+    ref = oracle.moe_forward(*x.args())
+    for o in outs:
+        err = assert_close(o.float().cpu().numpy(), ref, what=f"split tail T={T}")
+    assert torch.equal(outs[0], outs[1]) or (outs[0].float() - outs[1].float()).abs().max().item() < 1e-2
+    print(f"split tail T={T}: max_abs_err={err:.3e}")
+
+
 def test_all_paths_agree(pkg, gpu_inputs):
     x = gpu_inputs(64, seed=31)
     outs = []
