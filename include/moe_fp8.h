@@ -72,7 +72,7 @@ int moe_fp8_run_stage(const MoeFp8Args* args, int32_t stage, void* stream);
  *   1  weight-streaming GEMM1 + tile GEMM2,
  *   2  one weight-streaming launch doing GEMM1 and GEMM2 (decode shapes),
  *   3  weight-streaming GEMM1 and GEMM2 as two launches.
- * Automatic choice: 2 up to 384 tokens, 0 above. Plays the role of
+ * Automatic choice: 2 up to 240 tokens, 0 above. Plays the role of
  * the reference's token-count path selection (solution/triton/current_kernel.py:1812-1813, :2022). */
 int32_t moe_fp8_gemm_path(int32_t num_tokens);
 

@@ -176,7 +176,7 @@ struct Plan {
 //   2  one weight-streaming launch for GEMM1 and GEMM2 (fused queue)
 //   3  weight-streaming GEMM1 and GEMM2 as two launches
 // Automatic choice from measured crossovers on B200 (offset-0 routing, 32
-// local experts): the fused streaming launch up to 384 tokens, tile kernels above.
+// local experts): the fused streaming launch up to 240 tokens, tile kernels above.
 std::atomic<int> g_forced_path{-2};
 int gemm_path(int T) {
   int f = g_forced_path.load(std::memory_order_relaxed);
@@ -186,7 +186,7 @@ int gemm_path(int T) {
     g_forced_path.store(f, std::memory_order_relaxed);
   }
   if (f >= 0 && f <= 3) return f;
-  return T <= 384 ? 2 : 0;
+  return T <= 240 ? 2 : 0;
 }
 
 int make_plan(const MoeFp8Args* a, Plan& p) {

@@ -42,7 +42,7 @@ def test_kernels_per_call(pkg):
     assert lib.moe_fp8_kernels_per_call(0) == 0
     assert lib.moe_fp8_kernels_per_call(16) == 4        # routing, permute, fused streaming GEMMs, finalize
     assert lib.moe_fp8_kernels_per_call(4096) == 5
-    assert [lib.moe_fp8_gemm_path(t) for t in (1, 96, 384, 385, 4096)] == [2, 2, 2, 0, 0]
+    assert [lib.moe_fp8_gemm_path(t) for t in (1, 96, 240, 241, 4096)] == [2, 2, 2, 0, 0]
 
 
 def test_invalid_arguments_rejected_before_any_launch(pkg):
