@@ -202,6 +202,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmA2);
     tma_prefetch_desc(&tmW2);
   }
+  // Prologue work that needs nothing from the preceding kernels, so it runs
+  // while routing and the gather are still in flight:
+  //  * the first K-blocks of the weight tile this CTA will most likely start
+  //    with (queue order, every local expert hit once) go into L2, so HBM is
+  //    busy from the start;
+  //  * this CTA's share of the fp32 combine accumulator is zeroed; GEMM2 tiles
+  //    wait until every CTA has done its share.
+  if (args.prefetch_kb > 0 && warp == 1 && lane == 0) {
+    const int e = blockIdx.x / NT1, nt = blockIdx.x % NT1;
+    if (e < E)
+      for (int kb = 0; kb < args.prefetch_kb && kb < KB1; ++kb) {
+        tma_prefetch_l2_2d(&tmW13, kb * 128, e * kGemm1N + nt * 128);
+        tma_prefetch_l2_2d(&tmW13, kb * 128, e * kGemm1N + kInter + nt * 128);
+      }
+  }
+  if (args.zero_acc) {
+    const size_t n4 = (size_t)args.T * (kHidden / 4);
+    const size_t per = (n4 + gridDim.x - 1) / gridDim.x;
+    const size_t b0 = (size_t)blockIdx.x * per, b1 = min(n4, b0 + per);
+    float4* acc4 = reinterpret_cast<float4*>(args.out_acc);
+    for (size_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) acc4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __threadfence();
+  }
   pdl_trigger();
   pdl_wait();  // the expert histogram and operands come from the preceding kernels
   {
@@ -235,6 +258,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (args.zero_acc && threadIdx.x == 0) atomicAdd(args.zero_done, 1);   // after every thread's fenced zeroing
   const uint32_t tmem_base = S.tmem_base;
   const int total = mode == 1 ? S.tiles1 : mode == 2 ? S.tiles2 : S.tiles1 + S.tiles2;
 
@@ -242,6 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ producer: tile queue, tables, TMA
     if (lane == 0) {
       int it = 0;
+      bool zeroed = !args.zero_acc;
       for (int ti = 0;; ++ti) {
         const int p = ti & 1;
         if (!mbar_wait(smem_u32(&S.tab_empty[p]), ((ti >> 1) & 1) ^ 1)) {
@@ -265,6 +290,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           fence_proxy_async_global();
+        }
+        if (x.phase == 2 && !zeroed) {
+          // GEMM2 adds into the accumulator: every CTA's zeroing must be done
+          if (!wait_counter(args.zero_done, (int)gridDim.x)) {
+            set_abort(S, args.err, kErrTimeoutProducer);
+            S.tile_id[p] = kTileEnd;
+            mbar_arrive(tb);
+            break;
+          }
+          zeroed = true;
         }
         S.tile_id[p] = t;
         const int KB = x.phase == 1 ? KB1 : KB2;
@@ -478,6 +513,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (atomicAdd(args.queue + 1, 1) == (int)gridDim.x - 1) {
       atomicExch(args.queue, 0);
       atomicExch(args.queue + 1, 0);
+      if (args.zero_acc) atomicExch(args.zero_done, 0);
       if (mode == 3)
         for (int e = 0; e < E; ++e) atomicExch(args.done1 + e, 0);
     }

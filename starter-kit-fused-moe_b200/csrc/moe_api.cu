@@ -246,7 +246,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
       e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
                             a->local_expert_offset, E, a->routed_scaling_factor, p.topk_idx, p.topk_w, p.pair_pos,
-                            p.counts, p.acc, static_cast<__nv_bfloat16*>(a->output), st);
+                            p.counts, p.path >= 2 ? nullptr : p.acc, static_cast<__nv_bfloat16*>(a->output), st);
       if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
       break;
     case 1:
@@ -277,6 +277,10 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
         d.err = p.err;
         d.queue = reinterpret_cast<int*>(w + p.L.queue());
         d.done1 = reinterpret_cast<int*>(w + p.L.done1());
+        d.T = T;
+        d.zero_done = reinterpret_cast<int*>(w + p.L.zero_done());
+        d.zero_acc = d.mode != 1;            // this launch runs the GEMM2 tiles: it owns the zeroing
+        d.prefetch_kb = d.mode != 2 ? 16 : 0;
         e = moe::launch_stream_gemm(p.tmA1, p.tmB1, p.tmA2, p.tmB2, d, p.nsm, st);
         if (e != cudaSuccess) return cuda_fail(e, "streaming GEMM launch");
         break;

@@ -47,6 +47,10 @@ struct DecodeArgs {
   int* err;
   int* queue;              // [2]: tile counter, CTA exit counter (zero before the first launch)
   int* done1;              // [E]: finished GEMM1 tile parts per expert (mode 3)
+  int T;                   // tokens (rows of out_acc)
+  int zero_acc;            // zero out_acc in the prologue (GEMM2 tiles wait for every CTA's part)
+  int* zero_done;          // CTAs that finished zeroing (zero before the first launch)
+  int prefetch_kb;         // GEMM1 K-blocks per guessed first tile to prefetch into L2 in the prologue
 };
 cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13, const CUtensorMap& tmA2,
                                const CUtensorMap& tmW2, const DecodeArgs& args, int num_sms, cudaStream_t st);

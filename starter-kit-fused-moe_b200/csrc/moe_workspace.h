@@ -17,7 +17,8 @@ struct WsLayout {
   size_t err;                 // int32 error word (sticky; cleared by the host reader)
   size_t counts;              // int32 [E]   pairs per local expert, then the streaming kernel's
                               //             tile queue [2], per-expert GEMM1 progress [256] and
-                              //             the tile GEMM1's split-tile arrival counters [256]
+                              //             the tile GEMM1's split-tile arrival counters [256] and
+                              //             the streaming kernel's zeroing counter [1]
   size_t topk_idx;            // int32 [T*8] selected global experts (selection order)
   size_t topk_w;              // f32   [T*8] combine weights
   size_t pair_pos;            // int32 [T*8] position inside the expert's group, -1 if not local
@@ -33,7 +34,8 @@ struct WsLayout {
   size_t queue() const { return counts + sizeof(int32_t) * 256; }
   size_t done1() const { return counts + sizeof(int32_t) * 258; }
   size_t split_cnt() const { return counts + sizeof(int32_t) * 514; }
-  static constexpr size_t kCountersBytes = sizeof(int32_t) * (256 + 2 + 256 + 256);
+  size_t zero_done() const { return counts + sizeof(int32_t) * 770; }
+  static constexpr size_t kCountersBytes = sizeof(int32_t) * (256 + 2 + 256 + 256 + 4);
   static constexpr int kMaxSplitUnits = 160;
 };
 

@@ -14,7 +14,7 @@
 
 namespace moe {
 
-constexpr int kRouteWarps = 8;   // one token per warp, 8 tokens per block
+constexpr int kRouteWarps = 4;   // one token per warp, 4 tokens per block (a latency chain: spread it)
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
 
@@ -136,20 +136,19 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
         my_lpos = atomicAdd(&hist[le], 1);
       }
     }
-    // A token with a local expert gets a zeroed fp32 combine row (GEMM2 adds into
-    // it, finalize rounds it); a token without one is final already: zero output.
-    if (out_acc != nullptr) {
-      const bool has_local = __ballot_sync(0xffffffffu, my_le >= 0) != 0;
-      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (has_local) {
-        float4* row = reinterpret_cast<float4*>(out_acc + (size_t)t * kHidden);
+    // A token with a local expert gets a zeroed fp32 combine row when out_acc is
+    // given (GEMM2 adds into it, finalize rounds it; the streaming GEMM kernel
+    // zeroes it itself); a token without one is final already: zero output.
+    const bool has_local = __ballot_sync(0xffffffffu, my_le >= 0) != 0;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (has_local && out_acc != nullptr) {
+      float4* row = reinterpret_cast<float4*>(out_acc + (size_t)t * kHidden);
 #pragma unroll 4
-        for (int c = lane; c < kHidden / 4; c += 32) row[c] = z;
-      } else {
-        float4* row = reinterpret_cast<float4*>(out + (size_t)t * kHidden);
+      for (int c = lane; c < kHidden / 4; c += 32) row[c] = z;
+    } else if (!has_local && out != nullptr) {
+      float4* row = reinterpret_cast<float4*>(out + (size_t)t * kHidden);
 #pragma unroll 4
-        for (int c = lane; c < kHidden / 8; c += 32) row[c] = z;
-      }
+      for (int c = lane; c < kHidden / 8; c += 32) row[c] = z;
     }
   }
   __syncthreads();
@@ -187,8 +186,11 @@ __global__ void __launch_bounds__(256) permute_kernel(
     int* __restrict__ row_token, float* __restrict__ row_weight) {
   __shared__ int off[256];
   __shared__ int warp_sums[8];
-  pdl_wait();
+  // Let the GEMM kernel become resident now: its prologue (weight prefetch into
+  // L2, accumulator zeroing) overlaps routing and this gather; its own
+  // griddepcontrol.wait still waits for this grid, which waits for routing.
   pdl_trigger();
+  pdl_wait();
   padded_offsets_256(counts, E, off, warp_sums);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {

@@ -154,7 +154,8 @@ def test_all_paths_agree(pkg, gpu_inputs):
 
 
 def test_fused_path_repeated_and_stage_relaunch(pkg, oracle, gpu_inputs):
-    """The streaming kernel's tile queue re-arms itself: repeated calls and stage-alone re-launches."""
+    """The streaming kernel's tile queue and counters re-arm themselves: repeated calls and a
+    stage-alone re-launch (which zeroes and refills the combine accumulator) give the same output."""
     import bench
     x = gpu_inputs(40, seed=41)
     old = pkg.set_gemm_path(2)
@@ -162,12 +163,12 @@ def test_fused_path_repeated_and_stage_relaunch(pkg, oracle, gpu_inputs):
         op = bench.Op(pkg, x)
         for _ in range(3):
             op()
-        op.stage(2)            # fused GEMM1+GEMM2 again (adds a second copy into the accumulator)
+        op.stage(2)            # fused GEMM1+GEMM2 again: it zeroes the accumulator itself first
         op.stage(4)
         torch.cuda.synchronize()
         assert pkg.read_device_error() == 0
-        ref = oracle.moe_forward(*x.args(), out_dtype="f32") * 2
-        assert_close(op.out.float().cpu().numpy(), oracle.bf16_round(ref), what="stage relaunch")
+        ref = oracle.moe_forward(*x.args())
+        assert_close(op.out.float().cpu().numpy(), ref, what="stage relaunch")
     finally:
         pkg.set_gemm_path(old)
 
