@@ -14,9 +14,10 @@
 //   GEMM1 tile (expert, n1 in 0..15, token tile): W13 gate rows [128 n1, +128)
 //     and up rows [2048 + 128 n1, +128); epilogue SwiGLU and the two-term FP8
 //     re-quantisation of grouped_gemm.cu over the 128 columns the tile owns.
-//   GEMM2 tile (expert, n2 in 0..27, term tile of 8 pairs): W2 rows
-//     [256 n2, +256); epilogue sums each pair's hi/lo terms, scales by the
-//     routing weight and adds into the fp32 token accumulator.
+//   GEMM2 tile (expert, n2 in 0..27, term tile of 8 pairs, K half): W2 rows
+//     [256 n2, +256) over half of K; epilogue sums each pair's hi/lo terms,
+//     scales by the routing weight and adds into the fp32 token accumulator
+//     (the halves' partials simply add; half-size tiles shorten the tail).
 // Tiles come from a device-side queue (one atomic counter per launch), so the
 // work balances across SMs and, in the fused mode, GEMM2 tiles of an expert
 // start as soon as that expert's GEMM1 tiles are done: each GEMM1 tile bumps a
@@ -43,6 +44,7 @@ constexpr int NT1 = kInter / 128;        // 16 GEMM1 tiles per expert and token 
 constexpr int NT2 = kHidden / 256;       // 28 GEMM2 tiles per expert and term tile
 constexpr int KB1 = kHiddenBlocks;       // 56
 constexpr int KB2 = kInterBlocks;        // 16
+constexpr int KS2 = 2;                   // GEMM2 tiles are split in K (partials add into the accumulator)
 constexpr int kTileEnd = -1;
 
 struct Smem {
@@ -64,6 +66,7 @@ struct Smem {
   int row_off[kMaxLocalExperts];
   int cnt[kMaxLocalExperts];
   int tile_id[2];                        // tile of each table slot (kTileEnd = no more work)
+  unsigned long long tile_t0[2];         // claim time of each slot's tile (timeline builds)
   alignas(16) float sa[2][KB1][NTOK];    // activation scales of the tile's rows
   alignas(16) float sw[2][2][KB1];       // weight block scales of the tile's two 128-row blocks
   alignas(16) int tok[2][NTOK / 2];      // GEMM2: token and routing weight of the tile's pairs
@@ -76,7 +79,25 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 struct Tile {
   int phase;   // 1 or 2
   int e, nt, tt;
+  int k0, k1;  // K-blocks of the tile
 };
+
+// Optional per-tile timeline (built with -DMOE_GEMM_TRACE): CTA, queue index,
+// claim time and finish time (global timer, ns) of every tile.
+constexpr int kTileTraceMax = 8192;
+__device__ unsigned long long g_tile_trace[kTileTraceMax][4];
+__device__ int g_tile_trace_n;
+__device__ __forceinline__ void tile_trace(int t, unsigned long long t0) {
+#ifdef MOE_GEMM_TRACE
+  const int i = atomicAdd(&g_tile_trace_n, 1);
+  if (i < kTileTraceMax) {
+    g_tile_trace[i][0] = blockIdx.x;
+    g_tile_trace[i][1] = (unsigned long long)t;
+    g_tile_trace[i][2] = t0;
+    g_tile_trace[i][3] = globaltimer_ns();
+  }
+#endif
+}
 
 __device__ __forceinline__ int scan256(int v, int* warp_sums, int& total) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -120,13 +141,18 @@ __device__ __forceinline__ Tile decode_tile(const Smem& S, int E, int mode, int 
     const int local = t - S.start1[x.e];
     x.nt = local / S.tt1[x.e];
     x.tt = local - x.nt * S.tt1[x.e];
+    x.k0 = 0;
+    x.k1 = KB1;
   } else {
     t -= S.tiles1;
     x.phase = 2;
     x.e = find_expert(S.start2, E, t);
     const int local = t - S.start2[x.e];
-    x.nt = local / S.tt2[x.e];
-    x.tt = local - x.nt * S.tt2[x.e];
+    const int kh = local % KS2, rest = local / KS2;    // the K halves of a tile are adjacent in the queue
+    x.nt = rest / S.tt2[x.e];
+    x.tt = rest - x.nt * S.tt2[x.e];
+    x.k0 = kh * (KB2 / KS2);
+    x.k1 = x.k0 + KB2 / KS2;
   }
   return x;
 }
@@ -235,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     int tot0, tot1, tot2;
     const int roff = scan256(align_up(c, 128), S.warp_sums, tot0);
     const int s1 = scan256(t1 * NT1, S.warp_sums, tot1);
-    const int s2 = scan256(t2 * NT2, S.warp_sums, tot2);
+    const int s2 = scan256(t2 * NT2 * KS2, S.warp_sums, tot2);
     if (tid < E) {
       S.cnt[tid] = c;
       S.tt1[tid] = t1;
@@ -302,13 +328,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           zeroed = true;
         }
         S.tile_id[p] = t;
+        S.tile_t0[p] = globaltimer_ns();
         const int KB = x.phase == 1 ? KB1 : KB2;
         const size_t ld_sa = x.phase == 1 ? (size_t)args.R1 : 2 * (size_t)args.R1;
+        const int nk = x.k1 - x.k0;
         const int arow = (x.phase == 1 ? S.row_off[x.e] : 2 * S.row_off[x.e]) + x.tt * NTOK;
         const float* sa = x.phase == 1 ? args.sa1 : args.sa2;
-        const uint32_t bytes = KB * NTOK * 4 + 2 * KB * 4 + (x.phase == 2 ? NTOK * 4 : 0);
+        const uint32_t bytes = nk * NTOK * 4 + 2 * KB * 4 + (x.phase == 2 ? NTOK * 4 : 0);
         mbar_arrive_expect_tx(tb, bytes);
-        for (int kb = 0; kb < KB; ++kb)
+        for (int kb = x.k0; kb < x.k1; ++kb)
           bulk_load(smem_u32(&S.sa[p][kb][0]), sa + kb * ld_sa + arow, NTOK * 4, tb);
         if (x.phase == 1) {
           bulk_load(smem_u32(&S.sw[p][0][0]), args.s13 + ((size_t)x.e * 32 + x.nt) * KB1, KB1 * 4, tb);
@@ -326,7 +354,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int w0 = x.phase == 1 ? x.e * kGemm1N + x.nt * 128 : x.e * kHidden + x.nt * 256;
         const int w1 = x.phase == 1 ? x.e * kGemm1N + kInter + x.nt * 128 : w0 + 128;
         bool ok = true;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = x.k0; kb < x.k1; ++kb, ++it) {
           const int s = it % STAGES, u = it / STAGES;
           if (!mbar_wait(smem_u32(&S.empty[s]), (u & 1) ^ 1)) {
             set_abort(S, args.err, kErrTimeoutProducer);
@@ -357,7 +385,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int t = S.tile_id[p];
         mbar_arrive(smem_u32(&S.tab_empty[p]));
         if (t == kTileEnd) break;
-        const int KB = decode_tile(S, E, mode, t).phase == 1 ? KB1 : KB2;
+        const Tile x = decode_tile(S, E, mode, t);
+        const int KB = x.k1 - x.k0;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++it, ++kt) {
           const int s = it % STAGES, u = it / STAGES;
@@ -398,13 +427,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int t = S.tile_id[p];
       if (t == kTileEnd) break;
       const Tile x = decode_tile(S, E, mode, t);
-      const int KB = x.phase == 1 ? KB1 : KB2;
       const int nvalid = min(NTOK, (x.phase == 1 ? S.cnt[x.e] : 2 * S.cnt[x.e]) - x.tt * NTOK);
       float g[NTOK], u[NTOK];
 #pragma unroll
       for (int i = 0; i < NTOK; ++i) g[i] = u[i] = 0.f;
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb, ++kt) {
+      for (int kb = x.k0; kb < x.k1; ++kb, ++kt) {
         const int b = kt % NBUF, v = kt / NBUF;
         if (!mbar_wait(smem_u32(&S.tfull[b]), v & 1)) {
           set_abort(S, args.err, kErrTimeoutEpilogue);
@@ -497,6 +525,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       __syncwarp();
+      if (q == 0 && lane == 0) tile_trace(t, S.tile_t0[p]);
       if (lane == 0) mbar_arrive(smem_u32(&S.tab_empty[p]));
     }
   }
@@ -523,6 +552,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 static int g_attr_set[64];
 
 }  // namespace dec
+
+cudaError_t stream_trace(int enable, unsigned long long* host, int n) {
+  if (enable >= 0) {
+    static unsigned long long zeros[dec::kTileTraceMax][4];
+    const int z = 0;
+    cudaError_t e = cudaMemcpyToSymbol(dec::g_tile_trace_n, &z, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(dec::g_tile_trace, zeros, sizeof(zeros));
+    return e;
+  }
+  if (n > dec::kTileTraceMax * 4) n = dec::kTileTraceMax * 4;
+  return cudaMemcpyFromSymbol(host, dec::g_tile_trace, sizeof(unsigned long long) * n);
+}
 
 cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13, const CUtensorMap& tmA2,
                                const CUtensorMap& tmW2, const DecodeArgs& args, int num_sms, cudaStream_t st) {

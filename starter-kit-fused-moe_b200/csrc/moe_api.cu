@@ -421,6 +421,11 @@ int moe_fp8_debug_trace(int32_t enable, uint64_t* host, int32_t n) {
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "trace");
 }
 
+int moe_fp8_debug_stream_trace(int32_t enable, uint64_t* host, int32_t n) {
+  cudaError_t e = moe::stream_trace(enable, reinterpret_cast<unsigned long long*>(host), n);
+  return e == cudaSuccess ? MOE_OK : cuda_fail(e, "trace");
+}
+
 int moe_fp8_run_stage(const MoeFp8Args* a, int32_t stage, void* stream) {
   Plan p{};
   if (int rc = make_plan(a, p)) return rc;

@@ -66,6 +66,9 @@ cudaError_t launch_quantize(const void* x, bool bf16, int T, uint8_t* q, float* 
 // Text returned by moe_fp8_last_error() on the calling thread.
 void set_last_error(const char* msg);
 cudaError_t set_trace(int on);
+// Streaming kernel's per-tile timeline (trace builds): enable >= 0 clears it,
+// enable < 0 copies n words ([tiles][cta, queue index, claim ns, finish ns]) to host.
+cudaError_t stream_trace(int enable, unsigned long long* host, int n);
 cudaError_t read_trace(unsigned long long* host, int n);
 // tmOut: the GEMM2 operand viewed as [R1, 4096] bytes (hi row | lo row of
 // each pair), 32 x 64-byte boxes, 64-byte swizzle; GEMM1 stores its output tiles through it.
