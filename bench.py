@@ -34,9 +34,11 @@ W13_BYTES = 2 * I * H + 32 * 56 * 4                          # per expert, with 
 W2_BYTES = H * I + 56 * 16 * 4
 TOKEN_IO_BYTES = 256 * 4 + H + 56 * 4 + H * 2                # logits, hidden, scales, bf16 output
 L2_FLUSH_BYTES = 256 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
-# kernel at the default workload (T=64, seed 0), from the ncu summary in profiles/
-GEMM1_TRAFFIC_BYTES = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the kernel the
+# roofline line reports (seed 0 inputs): one ncu --set full capture each, summarised
+# in profiles/stream_gemm_kernel_decode_T64.md (T=64: the fused streaming launch)
+# and profiles/grouped_gemm_kernel_prefill_T4096.md (T=4096: the tile GEMM1).
+GEMM1_TRAFFIC_BYTES = {64: 763_864_064 + 8_500_736, 4096: 938_535_680 + 26_306_304}
 
 
 def load_peaks():
@@ -418,7 +420,8 @@ def main():
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_per_step, "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)",
         "data": "synthetic (seeded, benchmark distributions; random-init weights)",
-        "config": {"workload": f"decode T={T} tokens per GPU, E_local=32, local_expert_offset=0",
+        "config": {"workload": f"{'decode' if pkg.gemm_path(T) == 2 else 'prefill'} T={T} tokens per GPU, "
+                               "E_local=32, local_expert_offset=0",
                    "tokens": T, "local_experts": 32, "pairs": pairs, "hit_experts": hit,
                    "parallelism": "replicas" if world > 1 else "single",
                    "l2": "flushed (256 MB write) between timed calls; weights also exceed L2"},
