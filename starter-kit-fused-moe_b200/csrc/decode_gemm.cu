@@ -27,6 +27,7 @@
 // already claimed by running CTAs, so the wait cannot deadlock.
 #include "moe_common.cuh"
 #include "moe_kernels.h"
+#include "moe_workspace.h"
 
 namespace moe {
 namespace dec {
@@ -46,6 +47,10 @@ constexpr int KB1 = kHiddenBlocks;       // 56
 constexpr int KB2 = kInterBlocks;        // 16
 constexpr int KS2 = 2;                   // GEMM2 tiles are split in K (partials add into the accumulator)
 constexpr int kTileEnd = -1;
+constexpr int kMaxKSlices1 = 4;          // GEMM1 K-slices per tile at most (14 K-blocks each)
+// partial slices the workspace's split area holds (16 KB each) and tiles its counters cover
+constexpr int kMaxSplitSlots = (int)(WsLayout::kMaxSplitUnits * 128 * 256 * 4 / (EPI_WARPS * 2 * NTOK * 32 * 4));
+constexpr int kMaxSplitTiles = 256;
 
 struct Smem {
   uint64_t full[STAGES];
@@ -58,7 +63,9 @@ struct Smem {
   uint32_t tmem_base;
   int abort_flag;
   int warp_sums[8];
-  int tiles1, tiles2;                    // GEMM1 / GEMM2 tile counts of this launch
+  int tiles1, tiles2;                    // GEMM1 / GEMM2 tile counts of this launch (GEMM1 K-slices counted)
+  int ks1;                               // K-slices per GEMM1 tile (more than one when tiles are scarce)
+  int split_last[2];                     // GEMM1: this CTA's slice completed the tile
   int start1[kMaxLocalExperts + 1];      // GEMM1 tile prefix per expert
   int start2[kMaxLocalExperts + 1];
   int tt1[kMaxLocalExperts];             // token tiles per expert (GEMM1) / term tiles (GEMM2)
@@ -80,6 +87,7 @@ struct Tile {
   int phase;   // 1 or 2
   int e, nt, tt;
   int k0, k1;  // K-blocks of the tile
+  int kh;      // GEMM1: K-slice of the tile (0 when GEMM1 tiles are not split)
 };
 
 // Optional per-tile timeline (built with -DMOE_GEMM_TRACE): CTA, queue index,
@@ -139,10 +147,12 @@ __device__ __forceinline__ Tile decode_tile(const Smem& S, int E, int mode, int 
     x.phase = 1;
     x.e = find_expert(S.start1, E, t);
     const int local = t - S.start1[x.e];
-    x.nt = local / S.tt1[x.e];
-    x.tt = local - x.nt * S.tt1[x.e];
-    x.k0 = 0;
-    x.k1 = KB1;
+    const int ks = S.ks1, kh = local % ks, rest = local / ks;   // the K-slices of a tile are adjacent
+    x.nt = rest / S.tt1[x.e];
+    x.tt = rest - x.nt * S.tt1[x.e];
+    x.kh = kh;
+    x.k0 = kh * KB1 / ks;
+    x.k1 = (kh + 1) * KB1 / ks;
   } else {
     t -= S.tiles1;
     x.phase = 2;
@@ -153,6 +163,7 @@ __device__ __forceinline__ Tile decode_tile(const Smem& S, int E, int mode, int 
     x.tt = rest - x.nt * S.tt2[x.e];
     x.k0 = kh * (KB2 / KS2);
     x.k1 = x.k0 + KB2 / KS2;
+    x.kh = 0;
   }
   return x;
 }
@@ -262,19 +273,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int roff = scan256(align_up(c, 128), S.warp_sums, tot0);
     const int s1 = scan256(t1 * NT1, S.warp_sums, tot1);
     const int s2 = scan256(t2 * NT2 * KS2, S.warp_sums, tot2);
+    // Few GEMM1 tiles (a handful of hit experts): cut each into K-slices so
+    // every SM streams weights; the slices meet in a fix-up (the last one to
+    // arrive sums the fp32 partials and runs the epilogue).
+    int ks1 = 1;
+    if (args.split_partial != nullptr && tot1 > 0 && 2 * tot1 <= (int)gridDim.x && tot1 <= kMaxSplitTiles) {
+      // at most one round of slices (finer slicing at 4-8 tokens measured no gain)
+      ks1 = min(min((int)gridDim.x / tot1, kMaxKSlices1), kMaxSplitSlots / tot1);
+      if (ks1 < 2) ks1 = 1;
+    }
     if (tid < E) {
       S.cnt[tid] = c;
       S.tt1[tid] = t1;
       S.tt2[tid] = t2;
       S.row_off[tid] = roff;
-      S.start1[tid] = s1;
+      S.start1[tid] = s1 * ks1;
       S.start2[tid] = s2;
     }
     if (tid == 0) {
-      S.start1[E] = tot1;
+      S.start1[E] = tot1 * ks1;
       S.start2[E] = tot2;
-      S.tiles1 = tot1;
+      S.tiles1 = tot1 * ks1;
       S.tiles2 = tot2;
+      S.ks1 = ks1;
     }
   }
   if (warp == 1) {
@@ -457,7 +478,45 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!ok) break;
 
-      if (x.phase == 1) {
+      if (x.phase == 1 && S.ks1 > 1) {
+        // K-sliced GEMM1 tile: publish this slice's partial sums; the slice
+        // that completes the tile adds the others' and runs the epilogue
+        const int ks = S.ks1, base = t - x.kh;                  // queue index of the tile's slice 0
+        float* part = args.split_partial;
+        const size_t pb = ((size_t)t * EPI_WARPS + q) * (2 * NTOK) * 32 + lane;
+#pragma unroll
+        for (int i = 0; i < NTOK; ++i) {
+          __stcg(part + pb + (size_t)i * 32, g[i]);
+          __stcg(part + pb + (size_t)(NTOK + i) * 32, u[i]);
+        }
+        __threadfence();
+        if (!epi_sync(S, sync_uses, lane)) {
+          set_abort(S, args.err, kErrTimeoutEpilogue);
+          break;
+        }
+        if (q == 0 && lane == 0) {
+          const bool last = atomicAdd(args.split_cnt + base / ks, 1) == ks - 1;
+          if (last) atomicExch(args.split_cnt + base / ks, 0);   // re-armed for the next launch
+          S.split_last[p] = last;
+        }
+        if (!epi_sync(S, sync_uses, lane)) {
+          set_abort(S, args.err, kErrTimeoutEpilogue);
+          break;
+        }
+        if (S.split_last[p]) {
+          __threadfence();
+          for (int j = 0; j < ks; ++j) {
+            if (j == x.kh) continue;
+            const size_t ob = ((size_t)(base + j) * EPI_WARPS + q) * (2 * NTOK) * 32 + lane;
+#pragma unroll
+            for (int i = 0; i < NTOK; ++i) {
+              g[i] += __ldcg(part + ob + (size_t)i * 32);
+              u[i] += __ldcg(part + ob + (size_t)(NTOK + i) * 32);
+            }
+          }
+        }
+      }
+      if (x.phase == 1 && (S.ks1 == 1 || S.split_last[p])) {
         // C = silu(X2) * X1 for this thread's intermediate column and the tile's tokens
         float am[NTOK];
 #pragma unroll
@@ -512,7 +571,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           __syncwarp();
           if (lane == 0) atomicAdd(args.done1 + x.e, 1);
         }
-      } else {
+      } else if (x.phase == 2) {
         const int col = x.nt * 256 + r;
 #pragma unroll
         for (int i = 0; i < NTOK / 2; ++i) {

@@ -281,6 +281,8 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
         d.zero_done = reinterpret_cast<int*>(w + p.L.zero_done());
         d.zero_acc = d.mode != 1;            // this launch runs the GEMM2 tiles: it owns the zeroing
         d.prefetch_kb = d.mode != 2 ? 16 : 0;
+        d.split_partial = reinterpret_cast<float*>(w + p.L.split_partial);
+        d.split_cnt = reinterpret_cast<int*>(w + p.L.split_cnt());
         e = moe::launch_stream_gemm(p.tmA1, p.tmB1, p.tmA2, p.tmB2, d, p.nsm, st);
         if (e != cudaSuccess) return cuda_fail(e, "streaming GEMM launch");
         break;

@@ -51,6 +51,8 @@ struct DecodeArgs {
   int zero_acc;            // zero out_acc in the prologue (GEMM2 tiles wait for every CTA's part)
   int* zero_done;          // CTAs that finished zeroing (zero before the first launch)
   int prefetch_kb;         // GEMM1 K-blocks per guessed first tile to prefetch into L2 in the prologue
+  float* split_partial;    // fp32 partials of K-sliced GEMM1 tiles (null: no slicing)
+  int* split_cnt;          // arrivals per K-sliced GEMM1 tile (zero before the first launch)
 };
 cudaError_t launch_stream_gemm(const CUtensorMap& tmA1, const CUtensorMap& tmW13, const CUtensorMap& tmA2,
                                const CUtensorMap& tmW2, const DecodeArgs& args, int num_sms, cudaStream_t st);
