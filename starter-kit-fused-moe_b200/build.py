@@ -75,9 +75,47 @@ def build(debug: bool = False, verbose: bool = False, force: bool = False) -> pa
     return LIB
 
 
+TVM_SRC = HERE / "tvm_ffi" / "moe_tvm_ffi.cc"
+TVM_LIB = HERE / "libmoe_b200_tvm_ffi.so"
+
+
+def tvm_ffi_paths():
+    """(include dir, lib dir) of the installed apache-tvm-ffi package, or None."""
+    try:
+        import tvm_ffi
+    except ImportError:
+        return None
+    root = pathlib.Path(tvm_ffi.__file__).parent
+    inc, lib = root / "include", root / "lib"
+    return (inc, lib) if (inc / "tvm" / "ffi" / "function.h").exists() and (lib / "libtvm_ffi.so").exists() else None
+
+
+def build_tvm_ffi(force: bool = False) -> pathlib.Path | None:
+    """Build the TVM-FFI binding (`run`, the FlashInfer-Bench entry) over libmoe_b200.so.
+    Returns None when apache-tvm-ffi is not installed."""
+    paths = tvm_ffi_paths()
+    if paths is None:
+        return None
+    lib = build()
+    if not force and TVM_LIB.exists() and TVM_LIB.stat().st_mtime >= max(TVM_SRC.stat().st_mtime, lib.stat().st_mtime):
+        return TVM_LIB
+    inc, tlib = paths
+    cuda = pathlib.Path(nvcc()).parent.parent
+    cmd = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-fPIC", "-shared", str(TVM_SRC), "-o", str(TVM_LIB),
+           "-I", str(inc), "-I", str(INCLUDE), "-I", str(cuda / "include"),
+           "-L", str(HERE), "-lmoe_b200", "-L", str(tlib), "-ltvm_ffi", "-L", str(cuda / "lib64"), "-lcudart",
+           "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + str(tlib), "-Wl,-rpath," + str(cuda / "lib64")]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("TVM-FFI binding build failed")
+    return TVM_LIB
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--debug", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     print(build(debug=a.debug, verbose=a.verbose, force=True))
+    print(build_tvm_ffi(force=True))
