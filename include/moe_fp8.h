@@ -80,6 +80,17 @@ int32_t moe_fp8_gemm_path(int32_t num_tokens);
  * choice ($MOE_GEMM_PATH sets the initial value). Returns the previous setting. */
 int32_t moe_fp8_set_gemm_path(int32_t path);
 
+/* Deterministic combine (1) or the default fast combine (0); returns the
+ * previous setting ($MOE_DETERMINISTIC sets the initial value). When on, every
+ * call uses the 128-row tile kernels without K-sliced tiles, GEMM2 writes each
+ * (token, expert) output row once, and the final pass sums a token's rows in
+ * ascending local-expert order (the reference's accumulation order,
+ * ...json:146 step 3), so repeated calls give bit-identical outputs. The
+ * workspace then also holds those rows: moe_fp8_workspace_bytes reports the
+ * size for the current setting. Plays the role of the reference's ordered
+ * gather-reduce (cutlass_large_path.py:140-179). */
+int32_t moe_fp8_set_deterministic(int32_t on);
+
 /* Workspace bytes for up to `max_tokens` tokens and `num_local_experts` experts.
  * The reference keeps an equivalent op-owned cache (solution/cuda/kernel.cu:25-56,
  * solution/triton/current_kernel.py:186-208); here the caller owns it. */

@@ -68,7 +68,7 @@ EXPORTED_SYMBOLS = (
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
     "moe_fp8_set_gemm_path", "moe_fp8_gemm_path", "moe_fp8_route_static",
     "moe_fp8_ep_plan", "moe_fp8_ep_pack", "moe_fp8_ep_scales", "moe_fp8_ep_combine",
-    "moe_fp8_quantize_activations",
+    "moe_fp8_quantize_activations", "moe_fp8_set_deterministic",
 )
 
 _lib = None
@@ -104,6 +104,8 @@ def load_library(path: str | pathlib.Path | None = None) -> ctypes.CDLL:
         lib.moe_fp8_last_error.restype = ctypes.c_char_p
         lib.moe_fp8_set_gemm_path.argtypes = [i32]
         lib.moe_fp8_set_gemm_path.restype = i32
+        lib.moe_fp8_set_deterministic.argtypes = [i32]
+        lib.moe_fp8_set_deterministic.restype = i32
         lib.moe_fp8_gemm_path.argtypes = [i32]
         lib.moe_fp8_gemm_path.restype = i32
         lib.moe_fp8_debug_trace.argtypes = [i32, vp, i32]
@@ -285,6 +287,12 @@ def quantize_activations(x):
         _check(lib.moe_fp8_quantize_activations(_ptr(x), int(x.dtype == torch.bfloat16), T, _ptr(q), _ptr(s),
                                                 _stream_handle(x.device)), "moe_fp8_quantize_activations")
     return q, s
+
+
+def set_deterministic(on: bool) -> bool:
+    """Bit-reproducible combine (see moe_fp8_set_deterministic); returns the previous setting.
+    Workspaces obtained before the switch are re-sized on the next call."""
+    return bool(load_library().moe_fp8_set_deterministic(1 if on else 0))
 
 
 def set_gemm_path(path: int) -> int:

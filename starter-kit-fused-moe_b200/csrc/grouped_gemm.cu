@@ -300,7 +300,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         sp = min(min(G / tail, Cfg::MAX_SPLITS), (int)(WsLayout::kMaxSplitUnits / tail));
         if (sp < 2) sp = 1;
       }
-      if (sp == 1) tail = 0;
+      if (sp == 1 || args.no_split) {
+        sp = 1;
+        tail = 0;
+      }
       S.splits = sp;
       S.full_tiles = tot1 - tail;
       S.units = tot1 - tail + tail * sp;
@@ -471,8 +474,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int tok = lane < 16 ? S.row_tok[w][lane] : -1;
           if (tok >= 0) {
             const uint8_t* row = staging + (size_t)(w * 16 + lane) * Cfg::ROW_STRIDE;
-            float* dst = args.out_acc + (size_t)tok * kHidden + nt * BN + 128 * (w >> 2);
-            bulk_reduce_add_f32(dst, smem_u32(row), 128 * sizeof(float));
+            if (args.pair_out != nullptr) {
+              // deterministic mode: the pair's own row (staged row `lane` of epilogue
+              // warp w is pair 16 * quadrant + lane of the tile), written once
+              const size_t prow = (size_t)S.row_off[e] + mt * (BM / 2) + 16 * ((w + 2) & 3) + lane;
+              bulk_store(args.pair_out + prow * kHidden + nt * BN + 128 * (w >> 2), smem_u32(row), 128 * sizeof(float));
+            } else {
+              float* dst = args.out_acc + (size_t)tok * kHidden + nt * BN + 128 * (w >> 2);
+              bulk_reduce_add_f32(dst, smem_u32(row), 128 * sizeof(float));
+            }
             bulk_commit();
           }
           bulk_wait_read_all();

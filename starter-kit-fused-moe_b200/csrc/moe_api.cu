@@ -76,13 +76,14 @@ int num_sms_of_current_device() {
 }
 
 int gemm_path(int T);
+bool deterministic();
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 int check_workspace(void* ws, size_t bytes, int T, int E) {
   if (!ws) return fail(MOE_ERR_WORKSPACE, "workspace is NULL");
   if (!aligned(ws, 256)) return fail(MOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-  const size_t need = moe::ws_layout(T, E).total;
+  const size_t need = moe::ws_layout(T, E, deterministic()).total;
   if (bytes < need)
     return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes, got " +
                                        std::to_string(bytes));
@@ -99,7 +100,7 @@ const char* moe_fp8_last_error(void) { return g_last_error.c_str(); }
 
 size_t moe_fp8_workspace_bytes(int32_t max_tokens, int32_t num_local_experts) {
   if (max_tokens < 0 || num_local_experts < 1 || num_local_experts > moe::kMaxLocalExperts) return 0;
-  return moe::ws_layout(max_tokens, num_local_experts).total;
+  return moe::ws_layout(max_tokens, num_local_experts, deterministic()).total;
 }
 
 int32_t moe_fp8_kernels_per_call(int32_t num_tokens) {
@@ -168,6 +169,8 @@ struct Plan {
   uint8_t* a1; float* sa1; uint8_t* a2; float* sa2; float* acc; int* err;
   CUtensorMap tmA1, tmB1, tmA2, tmB2, tmO1;
   int path;  // see gemm_path()
+  bool det;  // deterministic combine (see moe_fp8_set_deterministic)
+  float* pair_out;
 };
 
 // GEMM kernel families per call:
@@ -177,8 +180,20 @@ struct Plan {
 //   3  weight-streaming GEMM1 and GEMM2 as two launches
 // Automatic choice from measured crossovers on B200 (offset-0 routing, 32
 // local experts): the fused streaming launch up to 240 tokens, tile kernels above.
+std::atomic<int> g_deterministic{-2};
+bool deterministic() {
+  int d = g_deterministic.load(std::memory_order_relaxed);
+  if (d == -2) {
+    const char* e = getenv("MOE_DETERMINISTIC");
+    d = (e && atoi(e) != 0) ? 1 : 0;
+    g_deterministic.store(d, std::memory_order_relaxed);
+  }
+  return d == 1;
+}
+
 std::atomic<int> g_forced_path{-2};
 int gemm_path(int T) {
+  if (deterministic()) return 0;     // the tile kernels are the ones with an ordered combine
   int f = g_forced_path.load(std::memory_order_relaxed);
   if (f == -2) {
     const char* e = getenv("MOE_GEMM_PATH");
@@ -207,7 +222,8 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
   if (int rc = check_workspace(a->workspace, a->workspace_bytes, T, E)) return rc;
   p.a = a;
   p.nsm = num_sms_of_current_device();
-  p.L = moe::ws_layout(T, E);
+  p.det = deterministic();
+  p.L = moe::ws_layout(T, E, p.det);
   const moe::WsLayout& L = p.L;
   uint8_t* w = static_cast<uint8_t*>(a->workspace);
   p.counts = reinterpret_cast<int*>(w + L.counts);
@@ -222,6 +238,7 @@ int make_plan(const MoeFp8Args* a, Plan& p) {
   p.sa2 = reinterpret_cast<float*>(w + L.sa2);
   p.acc = reinterpret_cast<float*>(w + L.out_acc);
   p.err = reinterpret_cast<int*>(w + L.err);
+  p.pair_out = p.det ? reinterpret_cast<float*>(w + L.pair_out) : nullptr;
   p.path = gemm_path(T);
   const bool s1 = p.path != 0, s2 = p.path >= 2;
   const uint32_t w2_box = s2 ? 128 : 256;
@@ -246,7 +263,8 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
       e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
                             a->local_expert_offset, E, a->routed_scaling_factor, p.topk_idx, p.topk_w, p.pair_pos,
-                            p.counts, p.path >= 2 ? nullptr : p.acc, static_cast<__nv_bfloat16*>(a->output), st);
+                            p.counts, (p.path >= 2 || p.det) ? nullptr : p.acc, static_cast<__nv_bfloat16*>(a->output),
+                            st);
       if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
       break;
     case 1:
@@ -318,6 +336,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
         g.sa2 = p.sa2;
         g.split_partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a->workspace) + p.L.split_partial);
         g.split_cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a->workspace) + p.L.split_cnt());
+        g.no_split = p.det;
         e = moe::launch_gemm1(p.tmA1, p.tmB1, p.tmO1, g, p.nsm, st);
       } else {
         g.sa = p.sa2;
@@ -325,12 +344,20 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
         g.row_token = p.row_token;
         g.row_weight = p.row_weight;
         g.out_acc = p.acc;
+        g.pair_out = p.pair_out;
+        g.no_split = p.det;
         e = moe::launch_gemm2(p.tmA2, p.tmB2, g, p.nsm, st);
       }
       if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
       break;
     }
     case 4:
+      if (p.det) {
+        e = moe::launch_finalize_ordered(p.pair_out, static_cast<__nv_bfloat16*>(a->output), T, p.topk_idx, p.pair_pos,
+                                         p.counts, a->local_expert_offset, E, st);
+        if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
+        break;
+      }
       e = moe::launch_finalize(p.acc, static_cast<__nv_bfloat16*>(a->output), T, p.topk_idx, a->local_expert_offset,
                                E, p.nsm, st);
       if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
@@ -363,6 +390,12 @@ int32_t moe_fp8_set_gemm_path(int32_t path) {
 }
 
 int32_t moe_fp8_gemm_path(int32_t num_tokens) { return gemm_path(num_tokens); }
+
+int32_t moe_fp8_set_deterministic(int32_t on) {
+  const int32_t old = deterministic() ? 1 : 0;
+  g_deterministic.store(on ? 1 : 0, std::memory_order_relaxed);
+  return old;
+}
 
 int moe_fp8_quantize_activations(const void* x, int32_t x_is_bf16, int32_t T, void* hidden_states,
                                  float* hidden_states_scale, void* stream) {

@@ -142,6 +142,13 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* dst, uint32_t src, ui
                "r"(src), "r"(bytes)
                : "memory");
 }
+// 1-D bulk copy shared -> global (16-byte aligned, size a multiple of 16),
+// tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(src), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until this thread's bulk groups have finished reading their shared-memory sources.
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }

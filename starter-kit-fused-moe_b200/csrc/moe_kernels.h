@@ -18,6 +18,8 @@ struct GemmArgs {
   const int* row_token;    // GEMM2: token of each pair row
   const float* row_weight; // GEMM2: routing weight of each pair row
   float* out_acc;          // GEMM2 out: f32 [T, 7168]
+  float* pair_out;         // GEMM2, deterministic mode: fp32 output row of every pair (no accumulation)
+  int no_split;            // deterministic mode: whole tiles only (no K-sliced tails)
   float* split_partial;    // GEMM1: fp32 partial tiles of K-split tail tiles
   int* split_cnt;          // GEMM1: arrivals per split tail tile (zero at launch)
   int* err;                // device error word
@@ -29,6 +31,10 @@ cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, 
 cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E, int offset, const int* topk_idx,
                            const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
                            float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st);
+// Deterministic combine: out[t] = bf16(sum of the token's pair rows of
+// pair_out in ascending local-expert order).
+cudaError_t launch_finalize_ordered(const float* pair_out, __nv_bfloat16* out, int T, const int* topk_idx,
+                                    const int* pair_pos, const int* counts, int offset, int E, cudaStream_t st);
 cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, const int* topk_idx, int offset, int E,
                             int num_sms, cudaStream_t st);
 // Weight-streaming GEMM kernel (decode_gemm.cu).

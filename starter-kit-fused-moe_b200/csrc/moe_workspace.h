@@ -30,6 +30,7 @@ struct WsLayout {
   size_t sa2;                 // f32   [16, 2*R1]   their 1x128 scales
   size_t out_acc;             // f32   [T, 7168]    combine accumulator
   size_t split_partial;       // f32   [kMaxSplitUnits, 128*256] tile GEMM1 K-split partial tiles
+  size_t pair_out;            // f32   [R1, 7168] per-pair GEMM2 outputs (deterministic mode only)
   size_t total;
   size_t queue() const { return counts + sizeof(int32_t) * 256; }
   size_t done1() const { return counts + sizeof(int32_t) * 258; }
@@ -41,7 +42,9 @@ struct WsLayout {
 
 inline size_t ws_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-inline WsLayout ws_layout(int T, int E) {
+// `deterministic` appends the per-pair output rows of the deterministic
+// combine; every other region keeps its offset.
+inline WsLayout ws_layout(int T, int E, bool deterministic = false) {
   WsLayout L{};
   L.T = T;
   L.E = E;
@@ -64,6 +67,7 @@ inline WsLayout ws_layout(int T, int E) {
   L.sa2 = take(sizeof(float) * 16 * 2 * (size_t)L.R1);
   L.out_acc = take(sizeof(float) * 7168 * (size_t)T);
   L.split_partial = take(sizeof(float) * 128 * 256 * (size_t)WsLayout::kMaxSplitUnits);
+  L.pair_out = deterministic ? take(sizeof(float) * 7168 * (size_t)L.R1) : 0;
   L.total = o;
   return L;
 }

@@ -263,6 +263,59 @@ __global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__
   }
 }
 
+// Deterministic combine: one warp per (token, 1024-column chunk) sums the
+// token's pair rows in ascending local-expert order, the order of the
+// reference's per-expert accumulation loop (...json:146, step 3), so the
+// result does not depend on which GEMM tile finished first.
+__global__ void __launch_bounds__(256) finalize_ordered_kernel(const float* __restrict__ pair_out,
+                                                               __nv_bfloat16* __restrict__ out, int T,
+                                                               const int* __restrict__ topk_idx,
+                                                               const int* __restrict__ pair_pos,
+                                                               const int* __restrict__ counts, int offset, int E) {
+  __shared__ int off[256];
+  __shared__ int warp_sums[8];
+  pdl_wait();
+  padded_offsets_256(counts, E, off, warp_sums);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const int le = lane < kTopK ? __ldg(topk_idx + (size_t)t * kTopK + lane) - offset : -1;
+  const bool local = le >= 0 && le < E;
+  const uint32_t lmask = __ballot_sync(0xffffffffu, local);
+  if (!lmask) return;
+  // rank of this lane's expert among the token's local experts (distinct ids)
+  int rank = 0;
+  for (int j = 0; j < kTopK; ++j) {
+    const int lj = __shfl_sync(0xffffffffu, le, j);
+    rank += ((lmask >> j) & 1) && lj < le;
+  }
+  const int row = local ? off[le] + __ldg(pair_pos + (size_t)t * kTopK + lane) : 0;
+  constexpr int kPer = kFinalizeChunk / 4 / 32;   // float4 per lane
+  float4 acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int n = __popc(lmask);
+  for (int r = 0; r < n; ++r) {
+    const int src = __ffs(__ballot_sync(0xffffffffu, local && rank == r)) - 1;
+    const int rr = __shfl_sync(0xffffffffu, row, src);
+    const float4* p = reinterpret_cast<const float4*>(pair_out + (size_t)rr * kHidden + blockIdx.y * kFinalizeChunk);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const float4 v = __ldg(p + lane + 32 * i);
+      acc[i].x += v.x;
+      acc[i].y += v.y;
+      acc[i].z += v.z;
+      acc[i].w += v.w;
+    }
+  }
+  __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + (size_t)t * kHidden + blockIdx.y * kFinalizeChunk);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    dst[2 * (lane + 32 * i)] = __floats2bfloat162_rn(acc[i].x, acc[i].y);
+    dst[2 * (lane + 32 * i) + 1] = __floats2bfloat162_rn(acc[i].z, acc[i].w);
+  }
+}
+
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
                          int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
@@ -282,6 +335,13 @@ cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E,
   if (grid > num_sms * 8) grid = num_sms * 8;
   return launch_kernel(permute_kernel, dim3(grid), dim3(256), 0, st, true, hidden, hs, T, E, offset, topk_idx, topk_w,
                        pair_pos, counts, R1, a1, sa1, row_token, row_weight);
+}
+
+cudaError_t launch_finalize_ordered(const float* pair_out, __nv_bfloat16* out, int T, const int* topk_idx,
+                                    const int* pair_pos, const int* counts, int offset, int E, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  return launch_kernel(finalize_ordered_kernel, dim3((T + 7) / 8, kHidden / kFinalizeChunk), dim3(256), 0, st, true,
+                       pair_out, out, T, topk_idx, pair_pos, counts, offset, E);
 }
 
 cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, const int* topk_idx, int offset, int E,

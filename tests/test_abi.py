@@ -72,3 +72,15 @@ def test_no_cpu_fallback_in_product_sources():
     """The product package never imports the oracle."""
     for p in (ROOT / "starter-kit-fused-moe_b200").rglob("*.py"):
         assert "moe_oracle" not in p.read_text() and "oracle/" not in p.read_text(), p
+
+
+def test_deterministic_switch_and_workspace(pkg):
+    lib = pkg.load_library()
+    base = lib.moe_fp8_workspace_bytes(64, 32)
+    old = pkg.set_deterministic(True)
+    try:
+        assert lib.moe_fp8_gemm_path(16) == 0                      # tile kernels only
+        assert lib.moe_fp8_workspace_bytes(64, 32) >= base + 64 * 7168 * 4
+    finally:
+        pkg.set_deterministic(old)
+    assert lib.moe_fp8_workspace_bytes(64, 32) == base
