@@ -186,6 +186,23 @@ def gemm2_bytes(pairs, hit):
     return hit * W2_BYTES + pairs * 2 * (I + 16 * 4) + pairs * H * 4 * 2
 
 
+def pinned_staging(tensors, align=256):
+    """One pinned host byte buffer holding `tensors` (each at a 256-byte aligned
+    offset), its device twin, and device views shaped like the tensors."""
+    offs, n = [], 0
+    for t in tensors:
+        n = (n + align - 1) // align * align
+        offs.append(n)
+        n += t.numel() * t.element_size()
+    host = torch.empty(n, dtype=torch.uint8).pin_memory()
+    for t, o in zip(tensors, offs):
+        b = t.detach().contiguous().cpu().view(torch.uint8).reshape(-1)
+        host[o:o + b.numel()].copy_(b)
+    dev = torch.empty(n, dtype=torch.uint8, device="cuda")
+    views = [dev[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape) for t, o in zip(tensors, offs)]
+    return host, dev, views
+
+
 def cpu_reference_time(pkg, O, x, max_seconds=60.0):
     """Time the oracle (numpy restatement of the definition's reference) on host cores."""
     xc = x.to("cpu")
@@ -391,17 +408,17 @@ def main():
         g1_bytes = gemm1_bytes(pairs, hit)
     g1_achieved = g1_bytes / (g1_ms * 1e-3) / 1e9
 
-    # ---- end to end through the public run(...) with host buffers
-    pin = lambda t: t.cpu().pin_memory()
-    h_logits, h_bias, h_hidden, h_hs = pin(x.routing_logits), pin(x.routing_bias), pin(x.hidden_states), \
-        pin(x.hidden_states_scale)
+    # ---- end to end through the public run(...) with host buffers: the step's
+    # inputs (logits, bias, FP8 hidden rows, scales) are staged in one pinned
+    # host buffer and moved with one host->device copy, as a serving loop would;
+    # run(...) gets device views into that buffer (each 256-byte aligned)
+    h_in, d_in_buf, d_in = pinned_staging((x.routing_logits, x.routing_bias, x.hidden_states,
+                                           x.hidden_states_scale))
     h_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    d_in = [torch.empty_like(t, device="cuda") for t in (h_logits, h_bias, h_hidden, h_hs)]
     d_out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
 
     def e2e_step():
-        for d, h in zip(d_in, (h_logits, h_bias, h_hidden, h_hs)):
-            d.copy_(h, non_blocking=True)
+        d_in_buf.copy_(h_in, non_blocking=True)
         pkg.run(d_in[0], d_in[1], d_in[2], d_in[3], x.gemm1_weights, x.gemm1_weights_scale, x.gemm2_weights,
                 x.gemm2_weights_scale, x.local_expert_offset, x.routed_scaling_factor, output=d_out)
         h_out.copy_(d_out, non_blocking=True)
@@ -412,7 +429,7 @@ def main():
     barrier(world)
     e2e_times = timed(e2e_step, a.steps, flush)
     e2e_ms = max_over_ranks(sum(e2e_times), world) / a.steps
-    h2d = sum(t.numel() * t.element_size() for t in (h_logits, h_bias, h_hidden, h_hs))
+    h2d = h_in.numel()
     d2h = h_out.numel() * h_out.element_size()
 
     line = {
