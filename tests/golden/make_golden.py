@@ -1,7 +1,7 @@
 """Generate golden vectors by running the reference operator itself.
 
 Runs only where the reference checkout is present (the build container):
-    python tests/golden/make_golden.py [--ref-root DIR] [--only name,name]
+    python tests/golden/make_golden.py --ref-root DIR [--only name,name]
 
 It execs the `reference` source of the operator definition
 (`resources/moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048.json:146`)
@@ -138,7 +138,7 @@ def make_routing_case(ref, name, logits, bias):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default="/root/reference")
+    ap.add_argument("--ref-root", required=True, help="checkout of the reference repository")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
     ref = load_reference(pathlib.Path(a.ref_root))
