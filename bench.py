@@ -34,11 +34,12 @@ W13_BYTES = 2 * I * H + 32 * 56 * 4                          # per expert, with 
 W2_BYTES = H * I + 56 * 16 * 4
 TOKEN_IO_BYTES = 256 * 4 + H + 56 * 4 + H * 2                # logits, hidden, scales, bf16 output
 L2_FLUSH_BYTES = 256 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the kernel the
-# roofline line reports (seed 0 inputs): one ncu --set full capture each, summarised
-# in profiles/stream_gemm_kernel_decode_T64.md (T=64: the fused streaming launch)
-# and profiles/grouped_gemm_kernel_prefill_T4096.md (T=4096: the tile GEMM1).
-GEMM1_TRAFFIC_BYTES = {64: 763_864_064 + 8_500_736, 4096: 938_535_680 + 26_306_304}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the fused
+# streaming kernel on the default workload (seed-0 inputs, T=64), from one
+# `ncu --set full --clock-control none -k regex:stream_gemm_kernel -s 2 -c 1`
+# capture of `python bench.py --steps 3 --warmup 3 --no-sweep --no-cpu-baseline`.
+# Other token counts have no capture, so their `traffic` is reported as null.
+STREAM_TRAFFIC_BYTES_T64 = 763_864_064 + 8_500_736
 
 
 def load_peaks():
@@ -50,9 +51,44 @@ def load_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def measure_fp8_peak(seconds=2.0):
+    """Dense FP8 tensor throughput of this GPU, measured live with the vendor
+    library: torch._scaled_mm (cuBLASLt) e4m3 x e4m3 -> bf16 at 8192^3, per-tensor
+    scales. Returns (burst TFLOP/s: best of 10 timed calls, sustained TFLOP/s:
+    back-to-back calls for `seconds`)."""
+    n = 8192
+    a = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn)
+    one = torch.ones((), device="cuda")
+    mm = lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    for _ in range(5):
+        mm()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        mm()
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    flop = 2.0 * n ** 3
+    reps = max(10, int(seconds * 1e3 / best))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        mm()
+    e1.record()
+    e1.synchronize()
+    sustained = flop * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+    del a, b
+    torch.cuda.empty_cache()
+    return flop / (best * 1e-3) / 1e12, sustained
+
+
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons sampled through NVML every
-    ~2 ms while the timed region runs (nvidia-smi as a fallback)."""
+    ~2 ms while the timed region runs."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
@@ -203,54 +239,67 @@ def pinned_staging(tensors, align=256):
     return host, dev, views
 
 
-def cpu_reference_time(pkg, O, x, max_seconds=60.0):
-    """Time the oracle (numpy restatement of the definition's reference) on host cores."""
+def cpu_reference_time(O, x, dequant_all=True):
+    """Seconds for one call of the CPU reference path: the numpy restatement of
+    the definition's PyTorch reference, dequantising every local expert first as
+    the reference does, with BLAS on all host cores."""
     xc = x.to("cpu")
     t0 = time.perf_counter()
-    O.moe_forward(*xc.args())
-    dt = time.perf_counter() - t0
-    return dt
+    O.moe_forward(*xc.args(), dequant_all=dequant_all)
+    return time.perf_counter() - t0
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else os.cpu_count()
+    except Exception:
+        return os.cpu_count()
 
 
 def run_reference_arm(a, world, rank):
-    """CPU reference path (the numpy oracle restating the definition's PyTorch
-    reference) on the host cores, on this arm's workload: the T-token decode call
-    at N=1; at N>1 the expert-parallel job (all ranks' tokens over 256 experts),
-    timed on a 64-token sample and scaled linearly to the job's token count."""
+    """CPU reference path on the host cores, on this arm's workload.
+
+    N=1: the T-token decode call (32 local experts) through the numpy
+    restatement of the definition's PyTorch reference, which dequantises all
+    local experts first as the reference does; every step is one full call.
+    BASELINE config 0 (T=16) is timed once alongside and reported in `config0`.
+    N>1: the expert-parallel job (N x 8192 tokens over 256 experts) needs tens of
+    fp32 TFLOP per step on the CPU; it is not timed, and no scaled estimate is
+    reported (an `unavailable` line)."""
     if rank != 0:
+        return
+    if world > 1:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"CPU reference of the {world} x {a.ep_tokens}-token expert-parallel step is not timed: "
+                          f"~{world * a.ep_tokens * 8 * FLOPS_PER_PAIR / 1e12:.0f} fp32 TFLOP per step on the host "
+                          "cores takes minutes, and no scaled estimate is reported"}), flush=True)
         return
     pkg = ge.load_package()
     O = ge.load_oracle()
-    if world == 1:
-        x = pkg.inputs.make_inputs(a.tokens, seed=0)
-        scale, sample = 1.0, f"full operator call at T={a.tokens}, 32 local experts"
-        workload = f"decode T={a.tokens} tokens per GPU, E_local=32, local_expert_offset=0"
-    else:
-        n = 64
-        x = pkg.inputs.make_inputs(n, seed=100, num_local_experts=256, weight_experts=8)
-        scale = world * a.ep_tokens / n
-        sample = (f"{n} tokens over all 256 experts, scaled x{scale:.0f} to {world} ranks x {a.ep_tokens} tokens "
-                  f"(linear in tokens)")
-        workload = f"expert parallel: {a.ep_tokens} tokens per GPU, 256 experts over {world} GPUs"
+    x = pkg.inputs.make_inputs(a.tokens, seed=0, num_local_experts=32)
+    workload = f"decode T={a.tokens} tokens per GPU, E_local=32, local_expert_offset=0"
     times = []
-    budget = 240.0
-    t_start = time.perf_counter()
     for i in range(a.warmup + a.steps):
-        dt = cpu_reference_time(pkg, O, x) * scale
+        dt = cpu_reference_time(O, x)
         if i >= a.warmup:
             times.append(dt)
-        if time.perf_counter() - t_start > budget and len(times) >= 1:
-            break
     us = statistics.median(times) * 1e6
-    cores = os.cpu_count()
+    x0 = pkg.inputs.make_inputs(16, seed=0)
+    t0 = statistics.median([cpu_reference_time(O, x0) for _ in range(3)]) * 1e6
+    cores = blas_threads()
     line = {"metric": "fused_moe_us_per_call", "value": us, "unit": "us", "n_gpus": world, "steps": len(times),
             "warmup": a.warmup, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, benchmark distributions)",
             "impl": "reference",
             "config": {"workload": workload, "parallelism": "cpu"},
+            "config0": {"workload": "BASELINE config 0: T=16, 32 local experts, seed 0", "us_per_call": t0,
+                        "calls": 3},
             "cpu_baseline": {"value": us, "unit": "us", "cores": cores, "kind": "port",
-                             "sample": sample + " (numpy restatement of the definition's PyTorch reference; "
-                                                "hit experts dequantised)"},
+                             "sample": f"one full operator call per step at T={a.tokens} (numpy restatement of the "
+                                       "definition's PyTorch reference; all 32 local experts dequantised to fp32 "
+                                       "first, as the reference does)"},
             "e2e": {"value": us, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -328,21 +377,45 @@ def run_ep_bench(a, world, rank):
         print(json.dumps(line), flush=True)
 
 
-def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, n=5, warm=3):
-    x = pkg.inputs.make_inputs(T, seed=seed, device="cuda", skewed=skewed)
+GEMM1_FLOPS_PER_PAIR = 2 * H * 2 * I
+GEMM2_FLOPS_PER_PAIR = 2 * I * H
+
+
+def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, fp8_peak, n=5, warm=3, E=32):
+    """One operator call configuration: whole-call time, per-GEMM stage-alone
+    times, and each against its roofline t_bound = max(bytes / HBM peak,
+    useful FLOPs / FP8 peak) (frac = t_bound / t)."""
+    x = pkg.inputs.make_inputs(T, seed=seed, device="cuda", skewed=skewed, num_local_experts=E)
     op = Op(pkg, x)
     for _ in range(warm):
         op()
     t = statistics.median(timed(op, n, flush))
     pairs, hit = op.routing_stats()
+    path = pkg.gemm_path(T)
     g1 = statistics.median(timed(lambda: op.stage(2), n, flush))
-    g2 = statistics.median(timed(lambda: op.stage(3), n, flush))
+    g2 = statistics.median(timed(lambda: op.stage(3), n, flush)) if path != 2 else 0.0
     b = algorithmic_bytes(T, pairs, hit)
     fl = pairs * FLOPS_PER_PAIR
-    res = {"T": T, "skewed": skewed, "us_per_call": t * 1e3, "pairs": pairs, "hit_experts": hit,
+    hbm = hbm_peak * 1e9
+    fp8 = fp8_peak * 1e12
+
+    def roof(bytes_, flops, ms):
+        tb = max(bytes_ / hbm, flops / fp8)
+        return {"us": ms * 1e3, "bytes": bytes_, "useful_flops": flops, "t_bound_us": tb * 1e6,
+                "bound": "hbm" if bytes_ / hbm >= flops / fp8 else "tensor",
+                "frac": tb / (ms * 1e-3), "tflops": flops / (ms * 1e-3) / 1e12,
+                "tensor_frac_of_fp8_peak": flops / (ms * 1e-3) / fp8}
+
+    res = {"T": T, "skewed": skewed, "local_experts": E, "us_per_call": t * 1e3, "pairs": pairs, "hit_experts": hit,
            "tflops": fl / (t * 1e-3) / 1e12, "hbm_gbs": b / (t * 1e-3) / 1e9,
            "hbm_frac_of_measured": b / (t * 1e-3) / 1e9 / hbm_peak,
-           "gemm1_us": g1 * 1e3, "gemm2_us": g2 * 1e3}
+           "roofline_call": roof(b, fl, t)}
+    if path == 2:
+        res["fused_stream_kernel"] = roof(gemm1_bytes(pairs, hit) + gemm2_bytes(pairs, hit), fl, g1)
+    else:
+        res["gemm1_kernel"] = roof(gemm1_bytes(pairs, hit), pairs * GEMM1_FLOPS_PER_PAIR, g1)
+        res["gemm2_kernel"] = roof(gemm2_bytes(pairs, hit), pairs * GEMM2_FLOPS_PER_PAIR, g2)
+        res["gemm2_kernel"]["mma_flops"] = 2 * pairs * GEMM2_FLOPS_PER_PAIR   # hi + lo terms of the intermediate
     del op, x
     torch.cuda.empty_cache()
     return res
@@ -375,6 +448,7 @@ def main():
 
     pkg = ge.load_package()
     hbm_peak, bf16_peak, peak_kind = load_peaks()
+    fp8_burst, fp8_sustained = measure_fp8_peak()
     T = a.tokens
     x = pkg.inputs.make_inputs(T, seed=rank, device="cuda")
     op = Op(pkg, x)
@@ -448,7 +522,10 @@ def main():
                      "achieved": g1_achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": g1_achieved / hbm_peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": g1_bytes, "launch_us": g1_ms * 1e3,
-                     "traffic": GEMM1_TRAFFIC_BYTES.get(T) if rank == 0 else None},
+                     "traffic": STREAM_TRAFFIC_BYTES_T64 if (T == 64 and path == 2) else None},
+        "peaks": {"hbm_gbs": hbm_peak, "hbm_kind": peak_kind, "fp8_tflops_burst": fp8_burst,
+                  "fp8_tflops_sustained": fp8_sustained,
+                  "fp8_how": "measured in this run: torch._scaled_mm e4m3 8192^3 (cuBLASLt), best of 10 / 2 s loop"},
         "e2e": {"value": e2e_ms * 1e3, "unit": "us", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": a.steps * int(pkg.load_library().moe_fp8_kernels_per_call(T)),
         "clocks": clk.summary(),
@@ -456,15 +533,19 @@ def main():
     del op
     if rank == 0 and world == 1 and not a.no_sweep:
         sw = []
-        for (tt, sk) in ((1, False), (8, False), (32, False), (4096, False), (16384, True)):
-            sw.append(sweep_point(pkg, tt, sk, 0, flush, hbm_peak))
+        # decode points, BASELINE configs 2 and 3, and the expert-parallel workload of one
+        # rank run on a single GPU holding all 256 experts (the like-for-like base of the EP lines);
+        # prefill points use the FP8 burst peak (each kernel is timed alone, milliseconds long)
+        for (tt, sk, e) in ((1, False, 32), (8, False, 32), (32, False, 32), (4096, False, 32), (16384, True, 32),
+                            (8192, False, 256)):
+            sw.append(sweep_point(pkg, tt, sk, 0 if e == 32 else 100, flush, hbm_peak, fp8_burst, E=e))
         line["sweep"] = sw
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         O = ge.load_oracle()
-        dt = cpu_reference_time(pkg, O, x)
-        line["cpu_baseline"] = {"value": dt * 1e6, "unit": "us", "cores": os.cpu_count(), "kind": "port",
+        dt = cpu_reference_time(O, x)
+        line["cpu_baseline"] = {"value": dt * 1e6, "unit": "us", "cores": blas_threads(), "kind": "port",
                                 "sample": f"one full operator call at T={T} (numpy restatement of the "
-                                          f"definition's PyTorch reference)"}
+                                          "definition's PyTorch reference, all local experts dequantised first)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

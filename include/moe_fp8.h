@@ -118,10 +118,24 @@ typedef struct MoeFp8WorkspaceView {
 int moe_fp8_workspace_view(void* workspace, int32_t num_tokens, int32_t num_local_experts,
                            MoeFp8WorkspaceView* view);
 
-/* Reads (and clears) the device error word of a workspace; synchronises `stream`.
- * Returns MOE_OK, or MOE_ERR_DEVICE_TIMEOUT with *bits set. The reference
- * checks CUDA errors after its launches (solution/cuda/kernel.cu:19-23). */
+/* Reads (and clears) the sticky device error word of a workspace; synchronises
+ * `stream`. Returns MOE_OK, or MOE_ERR_DEVICE_TIMEOUT with *bits set (1: a
+ * producer wait, 2: an MMA wait, 4: an epilogue wait ran out; 8: a debug-build
+ * index check failed). Every kernel that records an error also marks the
+ * current call, and that call's finalize pass writes NaN into the output rows
+ * it owns, so a failed call never returns plausible numbers even when nobody
+ * reads this word. The reference checks CUDA errors after its launches
+ * (solution/cuda/kernel.cu:19-23). */
 int moe_fp8_read_device_error(void* workspace, void* stream, int32_t* bits);
+
+/* Test hook for the bounded waits (affects every later launch in this process
+ * on the current device): `wait_limit_ns` replaces the 2 s limit of every
+ * device-side wait, and `gate_extra` is added to the target of the streaming
+ * kernel's GEMM2 gate (the count of finished GEMM1 tiles it waits for), so a
+ * test can make that wait run out without faulting anything. Restore with
+ * (2000000000, 0). Returns MOE_OK or MOE_ERR_INVALID_ARGUMENT / MOE_ERR_CUDA.
+ * Replaces nothing in the reference (its kernels have no bounded waits). */
+int moe_fp8_debug_set_waits(uint64_t wait_limit_ns, int32_t gate_extra);
 
 /* Routing without a workspace, for callers that may not allocate device
  * memory where they call this operator (a TensorRT plugin's enqueue, an XLA

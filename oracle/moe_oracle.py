@@ -13,8 +13,9 @@ source it follows. The restatement is pinned against golden vectors produced by
 running the reference itself (`tests/golden/make_golden.py`).
 
 Differences that do not change results:
-* only the experts that some token selects are dequantised (the reference
-  dequantises all of them first);
+* by default only the experts that some token selects are dequantised (the
+  reference dequantises all of them first; `dequant_all=True` does the same, for
+  timing the reference's cost);
 * fp32 matmuls go through numpy/BLAS rather than torch; the summation order of
   the fp32 dot products differs, which is far below the test tolerances.
 """
@@ -147,7 +148,7 @@ def route(logits: np.ndarray, bias: np.ndarray, routed_scaling_factor: float):
 def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                 gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                 local_expert_offset: int, routed_scaling_factor: float,
-                out_dtype: str = "bf16", routing=None):
+                out_dtype: str = "bf16", routing=None, dequant_all: bool = False):
     """Reference step "3) Local expert compute and accumulation".
 
     For every local expert that some token selected: G1 = A_e W13_e^T,
@@ -170,6 +171,11 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
     A = dequant_hidden(hq, hs) if T else np.zeros((0, H), np.float32)
     out = np.zeros((T, H), np.float32)
     off = int(local_expert_offset)
+    deq = None
+    if dequant_all:   # the reference's order: every local expert's weights first (step 1)
+        deq = [(dequant_block(fp8_bytes(gemm1_weights[le]), to_np(gemm1_weights_scale[le])),
+                dequant_block(fp8_bytes(gemm2_weights[le]), to_np(gemm2_weights_scale[le])))
+               for le in range(E_local)]
     for le in range(E_local):
         ge = off + le
         if ge < 0 or ge >= E_GLOBAL:
@@ -178,8 +184,11 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
         rows = np.nonzero(hit.any(axis=1))[0]
         if rows.size == 0:
             continue
-        w13 = dequant_block(fp8_bytes(gemm1_weights[le]), to_np(gemm1_weights_scale[le]))
-        w2 = dequant_block(fp8_bytes(gemm2_weights[le]), to_np(gemm2_weights_scale[le]))
+        if deq is not None:
+            w13, w2 = deq[le]
+        else:
+            w13 = dequant_block(fp8_bytes(gemm1_weights[le]), to_np(gemm1_weights_scale[le]))
+            w2 = dequant_block(fp8_bytes(gemm2_weights[le]), to_np(gemm2_weights_scale[le]))
         g1 = A[rows] @ w13.T
         x1, x2 = g1[:, :I], g1[:, I:]
         c = (x2 / (np.float32(1.0) + np.exp(-x2))) * x1

@@ -68,7 +68,7 @@ EXPORTED_SYMBOLS = (
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
     "moe_fp8_set_gemm_path", "moe_fp8_gemm_path", "moe_fp8_route_static",
     "moe_fp8_ep_plan", "moe_fp8_ep_pack", "moe_fp8_ep_scales", "moe_fp8_ep_combine",
-    "moe_fp8_quantize_activations", "moe_fp8_set_deterministic",
+    "moe_fp8_quantize_activations", "moe_fp8_set_deterministic", "moe_fp8_debug_set_waits",
 )
 
 _lib = None
@@ -110,6 +110,8 @@ def load_library(path: str | pathlib.Path | None = None) -> ctypes.CDLL:
         lib.moe_fp8_gemm_path.restype = i32
         lib.moe_fp8_debug_trace.argtypes = [i32, vp, i32]
         lib.moe_fp8_debug_trace.restype = ctypes.c_int
+        lib.moe_fp8_debug_set_waits.argtypes = [ctypes.c_uint64, i32]
+        lib.moe_fp8_debug_set_waits.restype = ctypes.c_int
         lib.moe_fp8_kernels_per_call.argtypes = [i32]
         lib.moe_fp8_kernels_per_call.restype = i32
         if path is None:

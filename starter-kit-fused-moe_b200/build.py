@@ -21,6 +21,11 @@ CSRC = HERE / "csrc"
 INCLUDE = HERE.parent / "include"
 LIB = HERE / "libmoe_b200.so"
 OBJ = HERE / "_build"
+# -DMOE_DEBUG build: every kernel checks its computed indices before the
+# accesses they guard and records error bit 8 instead of touching memory out of
+# range (compute-sanitizer is closed on the GPU pool, so this is the bounds check).
+DEBUG_LIB = HERE / "libmoe_b200_debug.so"
+DEBUG_OBJ = HERE / "_build_debug"
 
 
 def nvcc() -> str:
@@ -35,14 +40,16 @@ def _deps():
         sorted(INCLUDE.glob("*.h"))
 
 
-def up_to_date() -> bool:
-    return LIB.exists() and all(LIB.stat().st_mtime >= d.stat().st_mtime for d in _deps())
+def up_to_date(lib: pathlib.Path = LIB) -> bool:
+    return lib.exists() and all(lib.stat().st_mtime >= d.stat().st_mtime for d in _deps())
 
 
 def build(debug: bool = False, verbose: bool = False, force: bool = False) -> pathlib.Path:
-    if not force and up_to_date():
-        return LIB
-    OBJ.mkdir(exist_ok=True)
+    """Build libmoe_b200.so, or with `debug` the index-checking libmoe_b200_debug.so."""
+    lib_path, obj_dir = (DEBUG_LIB, DEBUG_OBJ) if debug else (LIB, OBJ)
+    if not force and up_to_date(lib_path):
+        return lib_path
+    obj_dir.mkdir(exist_ok=True)
     flags = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
              "-O3", "--expt-relaxed-constexpr", "-I", str(INCLUDE)]
     if debug:
@@ -52,7 +59,7 @@ def build(debug: bool = False, verbose: bool = False, force: bool = False) -> pa
     srcs = sorted(CSRC.glob("*.cu"))
 
     def compile_one(s):
-        o = OBJ / (s.stem + ".o")
+        o = obj_dir / (s.stem + ".o")
         r = subprocess.run([nvcc(), *flags, "-c", str(s), "-o", str(o)], capture_output=True, text=True)
         return s, o, r
 
@@ -65,14 +72,14 @@ def build(debug: bool = False, verbose: bool = False, force: bool = False) -> pa
         if r.returncode:
             raise RuntimeError(f"nvcc failed on {s.name}")
         objs.append(str(o))
-    tmp = LIB.with_name(LIB.name + ".tmp")
+    tmp = lib_path.with_name(lib_path.name + ".tmp")
     r = subprocess.run([nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(tmp), *objs,
                         "-lcudart"], capture_output=True, text=True)
     if r.returncode:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("link failed")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib_path)
+    return lib_path
 
 
 TVM_SRC = HERE / "tvm_ffi" / "moe_tvm_ffi.cc"
@@ -118,4 +125,5 @@ if __name__ == "__main__":
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     print(build(debug=a.debug, verbose=a.verbose, force=True))
-    print(build_tvm_ffi(force=True))
+    if not a.debug:
+        print(build_tvm_ffi(force=True))

@@ -169,7 +169,7 @@ __device__ __forceinline__ Tile decode_tile(const Smem& S, int E, int mode, int 
 }
 
 __device__ __forceinline__ void set_abort(Smem& S, int* err, int code) {
-  atomicOr(err, code);
+  record_error(err, code);
   *reinterpret_cast<volatile int*>(&S.abort_flag) = 1;
 }
 __device__ __forceinline__ bool aborted(const Smem& S) {
@@ -198,9 +198,9 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // Waits (bounded) until *p >= target with acquire semantics.
 __device__ __forceinline__ bool wait_counter(const int* p, int target) {
   if (ld_acquire(p) >= target) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long t0 = globaltimer_ns(), limit = g_wait_limit_ns;
   while (ld_acquire(p) < target) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit) return false;
     __nanosleep(64);
   }
   return true;
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const Tile x = decode_tile(S, E, mode, t);
         if (x.phase == 2 && mode == 3) {
           // GEMM2 reads this expert's SwiGLU rows: wait for all of its GEMM1 tiles
-          if (!wait_counter(args.done1 + x.e, EPI_WARPS * NT1 * S.tt1[x.e])) {
+          if (!wait_counter(args.done1 + x.e, EPI_WARPS * NT1 * S.tt1[x.e] + g_gate_extra)) {
             set_abort(S, args.err, kErrTimeoutProducer);
             S.tile_id[p] = kTileEnd;
             mbar_arrive(tb);
@@ -575,7 +575,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int col = x.nt * 256 + r;
 #pragma unroll
         for (int i = 0; i < NTOK / 2; ++i) {
-          if (2 * i < nvalid) {
+          if (2 * i < nvalid && MOE_DCHECK(S.tok[p][i] >= 0 && S.tok[p][i] < args.T, args.err)) {
             const float w = S.wgt[p][i];
             float* dst = args.out_acc + (size_t)S.tok[p][i] * kHidden + col;
             atomicAdd(dst, (g[2 * i] + g[2 * i + 1]) * w);
@@ -611,6 +611,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 static int g_attr_set[64];
 
 }  // namespace dec
+
+cudaError_t set_debug_waits_stream(unsigned long long limit_ns, int gate_extra) {
+  return set_debug_waits_here(limit_ns, gate_extra);
+}
 
 cudaError_t stream_trace(int enable, unsigned long long* host, int n) {
   if (enable >= 0) {

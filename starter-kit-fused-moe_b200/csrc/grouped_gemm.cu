@@ -216,7 +216,7 @@ __device__ __forceinline__ Unit unit_of(const GemmSmem& S, int u, int KB) {
 }
 
 __device__ __forceinline__ void set_abort(GemmSmem& S, int* err, int code) {
-  atomicOr(err, code);
+  record_error(err, code);
   *reinterpret_cast<volatile int*>(&S.abort_flag) = 1;
 }
 __device__ __forceinline__ bool aborted(const GemmSmem& S) {
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           const int tok = lane < 16 ? S.row_tok[w][lane] : -1;
-          if (tok >= 0) {
+          if (tok >= 0 && MOE_DCHECK(tok < args.T, args.err)) {
             const uint8_t* row = staging + (size_t)(w * 16 + lane) * Cfg::ROW_STRIDE;
             if (args.pair_out != nullptr) {
               // deterministic mode: the pair's own row (staged row `lane` of epilogue
@@ -662,7 +662,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
+        if (lane == 0 && MOE_DCHECK(row_off_e + mt * BM + 32 * q + 32 <= args.R1, args.err)) {
           const int y = row_off_e + mt * BM + 32 * q;         // pair row of the warp's first row
           tma_store_2d(&tmOut, smem_u32(box_hi), nt * 128 + 64 * g, y);
           tma_store_2d(&tmOut, smem_u32(box_lo), kInter + nt * 128 + 64 * g, y);
@@ -738,6 +738,10 @@ cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
   }
   return launch_kernel(grouped_gemm_kernel<MODE>, dim3(num_sms), dim3(GEMM_THREADS), gemm_smem_bytes<MODE>(), st, true, tmA,
                        tmB, tmOut, args);
+}
+
+cudaError_t set_debug_waits_tile(unsigned long long limit_ns, int gate_extra) {
+  return set_debug_waits_here(limit_ns, gate_extra);
 }
 
 cudaError_t set_trace(int on) {

@@ -259,7 +259,8 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
   cudaError_t e = cudaSuccess;
   switch (stage) {
     case 0:
-      e = cudaMemsetAsync(p.counts, 0, moe::WsLayout::kCountersBytes, st);
+      // one memset: the call's error word (word 1 of the error area) through the counter block
+      e = cudaMemsetAsync(p.err + 1, 0, p.L.counts + moe::WsLayout::kCountersBytes - p.L.err - sizeof(int), st);
       if (e != cudaSuccess) return cuda_fail(e, "clearing expert counts");
       e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
                             a->local_expert_offset, E, a->routed_scaling_factor, p.topk_idx, p.topk_w, p.pair_pos,
@@ -270,7 +271,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
     case 1:
       e = moe::launch_permute(static_cast<const uint8_t*>(a->hidden_states), a->hidden_states_scale, T, E,
                               a->local_expert_offset, p.topk_idx, p.topk_w, p.pair_pos, p.counts, p.L.R1, p.a1,
-                              p.sa1, p.row_token, p.row_weight, p.nsm, st);
+                              p.sa1, p.row_token, p.row_weight, p.err, p.nsm, st);
       if (e != cudaSuccess) return cuda_fail(e, "permute kernel launch");
       break;
     case 2:
@@ -329,6 +330,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       g.E = E;
       g.R1 = p.L.R1;
       g.err = p.err;
+      g.T = T;
       if (stage == 2) {
         g.sa = p.sa1;
         g.sb = a->gemm1_weights_scale;
@@ -354,12 +356,12 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
     case 4:
       if (p.det) {
         e = moe::launch_finalize_ordered(p.pair_out, static_cast<__nv_bfloat16*>(a->output), T, p.topk_idx, p.pair_pos,
-                                         p.counts, a->local_expert_offset, E, st);
+                                         p.counts, a->local_expert_offset, E, p.err, st);
         if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
         break;
       }
       e = moe::launch_finalize(p.acc, static_cast<__nv_bfloat16*>(a->output), T, p.topk_idx, a->local_expert_offset,
-                               E, p.nsm, st);
+                               E, p.err, st);
       if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
       break;
     default:
@@ -448,6 +450,13 @@ int moe_fp8_ep_combine(const void* returned_partials, const int32_t* slot, const
                                          wave_tokens, T, world, static_cast<__nv_bfloat16*>(output),
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "ep_combine");
+}
+
+int moe_fp8_debug_set_waits(uint64_t wait_limit_ns, int32_t gate_extra) {
+  if (wait_limit_ns == 0 || gate_extra < 0) return fail(MOE_ERR_INVALID_ARGUMENT, "debug_set_waits: bad arguments");
+  cudaError_t e = moe::set_debug_waits_stream(wait_limit_ns, gate_extra);
+  if (e == cudaSuccess) e = moe::set_debug_waits_tile(wait_limit_ns, gate_extra);
+  return e == cudaSuccess ? MOE_OK : cuda_fail(e, "debug_set_waits");
 }
 
 // Profiling aid: timeline of the GEMM kernels' CTA 0 (see grouped_gemm.cu).

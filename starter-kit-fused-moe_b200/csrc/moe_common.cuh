@@ -40,6 +40,36 @@ constexpr int kErrTimeoutEpilogue = 4;
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Set when a kernel found an index outside its buffer (debug builds only,
+// -DMOE_DEBUG); the access is skipped.
+constexpr int kErrIndex = 8;
+
+// The device error area (first 256 bytes of the workspace): word 0 is sticky
+// (cleared only by the host reader), word 1 covers the current call (cleared
+// with the call's counters); the finalize pass reads word 1.
+__device__ __forceinline__ void record_error(int* err, int code) {
+  atomicOr(err, code);
+  atomicOr(err + 1, code);
+}
+
+// Test hooks, one copy per translation unit (set from the host through
+// moe_fp8_debug_set_waits): the wait limit, and an amount added to the
+// streaming kernel's GEMM2 gate target so that a test can make that wait run
+// out on purpose. Defaults: 2 s, 0.
+static __device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+static __device__ int g_gate_extra = 0;
+static inline cudaError_t set_debug_waits_here(unsigned long long limit_ns, int gate_extra) {
+  cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &limit_ns, sizeof(limit_ns));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_gate_extra, &gate_extra, sizeof(gate_extra));
+  return e;
+}
+
+#ifdef MOE_DEBUG
+// Debug builds check computed indices before the access they guard.
+#define MOE_DCHECK(cond, err) ((cond) ? true : (record_error((err), kErrIndex), false))
+#else
+#define MOE_DCHECK(cond, err) true
+#endif
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -84,13 +114,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Gives up after
-// kWaitLimitNs and returns false (the caller records an error and unwinds).
+// g_wait_limit_ns (2 s) and returns false (the caller records an error and unwinds).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long t0 = globaltimer_ns(), limit = g_wait_limit_ns;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit) return false;
   }
 }
 

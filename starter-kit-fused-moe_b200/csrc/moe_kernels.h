@@ -23,6 +23,7 @@ struct GemmArgs {
   float* split_partial;    // GEMM1: fp32 partial tiles of K-split tail tiles
   int* split_cnt;          // GEMM1: arrivals per split tail tile (zero at launch)
   int* err;                // device error word
+  int T;                   // tokens (rows of out_acc), for the debug-build index checks
 };
 
 cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
@@ -30,13 +31,15 @@ cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, 
                          __nv_bfloat16* out, cudaStream_t st);
 cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E, int offset, const int* topk_idx,
                            const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
-                           float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st);
+                           float* sa1, int* row_token, float* row_weight, int* err, int num_sms, cudaStream_t st);
 // Deterministic combine: out[t] = bf16(sum of the token's pair rows of
 // pair_out in ascending local-expert order).
+// Both finalize passes write NaN rows when the call's error word (err[1]) is set.
 cudaError_t launch_finalize_ordered(const float* pair_out, __nv_bfloat16* out, int T, const int* topk_idx,
-                                    const int* pair_pos, const int* counts, int offset, int E, cudaStream_t st);
+                                    const int* pair_pos, const int* counts, int offset, int E, const int* err,
+                                    cudaStream_t st);
 cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, const int* topk_idx, int offset, int E,
-                            int num_sms, cudaStream_t st);
+                            const int* err, cudaStream_t st);
 // Weight-streaming GEMM kernel (decode_gemm.cu).
 struct DecodeArgs {
   int mode;                // 1: GEMM1 tiles, 2: GEMM2 tiles, 3: both in one launch
@@ -71,6 +74,9 @@ cudaError_t launch_ep_scales(const float* src, int N, float* dst, cudaStream_t s
 cudaError_t launch_ep_combine(const __nv_bfloat16* back, const int* slot, const int* send_off, int wave_tokens, int T,
                               int W, __nv_bfloat16* out, cudaStream_t st);
 cudaError_t launch_quantize(const void* x, bool bf16, int T, uint8_t* q, float* scale, cudaStream_t st);
+// Test hooks of the bounded waits (one per translation unit with waits).
+cudaError_t set_debug_waits_stream(unsigned long long limit_ns, int gate_extra);
+cudaError_t set_debug_waits_tile(unsigned long long limit_ns, int gate_extra);
 // Text returned by moe_fp8_last_error() on the calling thread.
 void set_last_error(const char* msg);
 cudaError_t set_trace(int on);

@@ -37,6 +37,8 @@ struct WsLayout {
   size_t split_cnt() const { return counts + sizeof(int32_t) * 514; }
   size_t zero_done() const { return counts + sizeof(int32_t) * 770; }
   static constexpr size_t kCountersBytes = sizeof(int32_t) * (256 + 2 + 256 + 256 + 4);
+  // Every counter accessor must land inside the block that ws_layout reserves.
+  static_assert(sizeof(int32_t) * (770 + 1) <= kCountersBytes, "counter block too small");
   static constexpr int kMaxSplitUnits = 160;
 };
 
@@ -55,7 +57,7 @@ inline WsLayout ws_layout(int T, int E, bool deterministic = false) {
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t r = o; o = ws_align(o + bytes, 1024); return r; };
   L.err = take(256);
-  L.counts = take(sizeof(int32_t) * (256 + 2 + 256));
+  L.counts = take(WsLayout::kCountersBytes);
   L.topk_idx = take(sizeof(int32_t) * 8 * (size_t)T);
   L.topk_w = take(sizeof(float) * 8 * (size_t)T);
   L.pair_pos = take(sizeof(int32_t) * 8 * (size_t)T);

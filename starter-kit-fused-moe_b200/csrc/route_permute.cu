@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(256) permute_kernel(
     const uint8_t* __restrict__ hidden, const float* __restrict__ hs, int T, int E, int offset,
     const int* __restrict__ topk_idx, const float* __restrict__ topk_w, const int* __restrict__ pair_pos,
     const int* __restrict__ counts, int R1, uint8_t* __restrict__ a1, float* __restrict__ sa1,
-    int* __restrict__ row_token, float* __restrict__ row_weight) {
+    int* __restrict__ row_token, float* __restrict__ row_weight, int* __restrict__ err) {
   __shared__ int off[256];
   __shared__ int warp_sums[8];
   // Let the GEMM kernel become resident now: its prologue (weight prefetch into
@@ -219,6 +219,7 @@ __global__ void __launch_bounds__(256) permute_kernel(
       const int kge = __shfl_sync(0xffffffffu, ge, k);
       const float kw = __shfl_sync(0xffffffffu, w, k);
       const int row = off[kge - offset] + kpp;
+      if (!MOE_DCHECK(kge - offset >= 0 && kge - offset < E && row >= 0 && row < R1, err)) continue;
       uint4* dst = reinterpret_cast<uint4*>(a1 + (size_t)row * kHidden);
 #pragma unroll
       for (int i = 0; i < kPer; ++i) dst[lane + 32 * i] = v[i];
@@ -232,12 +233,20 @@ __global__ void __launch_bounds__(256) permute_kernel(
   }
 }
 
+// A call whose kernels recorded an error (a bounded wait ran out, or a debug
+// index check failed) must not return plausible numbers: its finalize pass
+// writes NaN into every row it owns.
+__device__ __forceinline__ bool call_failed(const int* err) {
+  return *reinterpret_cast<const volatile int*>(err + 1) != 0;
+}
+
 // out[t] = bf16(acc[t]) for the tokens with a local expert (the routing kernel
 // already wrote zeros for the others). One warp per (token, 1024-column chunk);
 // each lane issues all of its loads before converting.
 constexpr int kFinalizeChunk = 1024;
 __global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out,
-                                                       int T, const int* __restrict__ topk_idx, int offset, int E) {
+                                                       int T, const int* __restrict__ topk_idx, int offset, int E,
+                                                       const int* __restrict__ err) {
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
@@ -249,10 +258,12 @@ __global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__
   uint4* dst = reinterpret_cast<uint4*>(out + base);
   constexpr int kPer = kFinalizeChunk / 8 / 32;  // 4 groups of 8 per lane
   float4 v[2 * kPer];
+  const bool failed = call_failed(err);
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     v[2 * i] = __ldg(src + 2 * (lane + 32 * i));
     v[2 * i + 1] = __ldg(src + 2 * (lane + 32 * i) + 1);
+    if (failed) v[2 * i] = v[2 * i + 1] = make_float4(NAN, NAN, NAN, NAN);
   }
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
@@ -271,7 +282,8 @@ __global__ void __launch_bounds__(256) finalize_ordered_kernel(const float* __re
                                                                __nv_bfloat16* __restrict__ out, int T,
                                                                const int* __restrict__ topk_idx,
                                                                const int* __restrict__ pair_pos,
-                                                               const int* __restrict__ counts, int offset, int E) {
+                                                               const int* __restrict__ counts, int offset, int E,
+                                                               const int* __restrict__ err) {
   __shared__ int off[256];
   __shared__ int warp_sums[8];
   pdl_wait();
@@ -298,6 +310,7 @@ __global__ void __launch_bounds__(256) finalize_ordered_kernel(const float* __re
   for (int r = 0; r < n; ++r) {
     const int src = __ffs(__ballot_sync(0xffffffffu, local && rank == r)) - 1;
     const int rr = __shfl_sync(0xffffffffu, row, src);
+    if (!MOE_DCHECK(rr >= 0 && rr < 8 * T + 128 * E, const_cast<int*>(err))) continue;
     const float4* p = reinterpret_cast<const float4*>(pair_out + (size_t)rr * kHidden + blockIdx.y * kFinalizeChunk);
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
@@ -309,6 +322,9 @@ __global__ void __launch_bounds__(256) finalize_ordered_kernel(const float* __re
     }
   }
   __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + (size_t)t * kHidden + blockIdx.y * kFinalizeChunk);
+  if (call_failed(err))
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) acc[i] = make_float4(NAN, NAN, NAN, NAN);
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     dst[2 * (lane + 32 * i)] = __floats2bfloat162_rn(acc[i].x, acc[i].y);
@@ -329,27 +345,27 @@ cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, 
 
 cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E, int offset, const int* topk_idx,
                            const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
-                           float* sa1, int* row_token, float* row_weight, int num_sms, cudaStream_t st) {
+                           float* sa1, int* row_token, float* row_weight, int* err, int num_sms, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   int grid = (T + 7) / 8;
   if (grid > num_sms * 8) grid = num_sms * 8;
   return launch_kernel(permute_kernel, dim3(grid), dim3(256), 0, st, true, hidden, hs, T, E, offset, topk_idx, topk_w,
-                       pair_pos, counts, R1, a1, sa1, row_token, row_weight);
+                       pair_pos, counts, R1, a1, sa1, row_token, row_weight, err);
 }
 
 cudaError_t launch_finalize_ordered(const float* pair_out, __nv_bfloat16* out, int T, const int* topk_idx,
-                                    const int* pair_pos, const int* counts, int offset, int E, cudaStream_t st) {
+                                    const int* pair_pos, const int* counts, int offset, int E, const int* err,
+                                    cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   return launch_kernel(finalize_ordered_kernel, dim3((T + 7) / 8, kHidden / kFinalizeChunk), dim3(256), 0, st, true,
-                       pair_out, out, T, topk_idx, pair_pos, counts, offset, E);
+                       pair_out, out, T, topk_idx, pair_pos, counts, offset, E, err);
 }
 
 cudaError_t launch_finalize(const float* acc, __nv_bfloat16* out, int T, const int* topk_idx, int offset, int E,
-                            int num_sms, cudaStream_t st) {
+                            const int* err, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  (void)num_sms;
   return launch_kernel(finalize_kernel, dim3((T + 7) / 8, kHidden / kFinalizeChunk), dim3(256), 0, st, true, acc, out,
-                       T, topk_idx, offset, E);
+                       T, topk_idx, offset, E, err);
 }
 
 }  // namespace moe

@@ -60,7 +60,7 @@ void* workspace_for(int device, size_t need) {
 
 void run(TensorView routing_logits, TensorView routing_bias, TensorView hidden_states, TensorView hidden_states_scale,
          TensorView gemm1_weights, TensorView gemm1_weights_scale, TensorView gemm2_weights,
-         TensorView gemm2_weights_scale, int64_t local_expert_offset, double routed_scaling_factor,
+         TensorView gemm2_weights_scale, int32_t local_expert_offset, float routed_scaling_factor,
          TensorView output) {
   expect(routing_logits.device().device_type == kDLCUDA, "routing_logits must be a CUDA tensor");
   const int dev = routing_logits.device().device_id;
@@ -103,8 +103,8 @@ void run(TensorView routing_logits, TensorView routing_bias, TensorView hidden_s
   a.gemm1_weights_scale = static_cast<const float*>(gemm1_weights_scale.data_ptr());
   a.gemm2_weights = gemm2_weights.data_ptr();
   a.gemm2_weights_scale = static_cast<const float*>(gemm2_weights_scale.data_ptr());
-  a.local_expert_offset = (int32_t)local_expert_offset;
-  a.routed_scaling_factor = (float)routed_scaling_factor;
+  a.local_expert_offset = local_expert_offset;
+  a.routed_scaling_factor = routed_scaling_factor;
   a.output = output.data_ptr();
   a.num_tokens = (int32_t)T;
   a.num_local_experts = (int32_t)E;

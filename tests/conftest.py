@@ -55,3 +55,27 @@ def same_selection(idx_a, idx_b, sb):
         vb = np.sort(sb[t, idx_b[t]])
         same[t] = np.array_equal(va, vb)
     return same
+
+
+def sampled_rows(oracle, x, n=160, seed=1234):
+    """Token rows to check a large call on (the operator is token-wise): every
+    token with >= 4 local experts (at most n // 2 of them), the first and last
+    token, and a seeded random draw up to n rows. Returns (rows int64 numpy,
+    MoeInputs of those tokens on the CPU, with the same weights)."""
+    import torch
+    from dataclasses import replace
+    logits = oracle.to_np(x.routing_logits)
+    bias = oracle.to_np(x.routing_bias)
+    idx, _ = oracle.route(logits, bias, x.routed_scaling_factor)
+    E = int(x.gemm1_weights.shape[0])
+    le = idx - int(x.local_expert_offset)
+    nloc = ((le >= 0) & (le < E)).sum(axis=1)
+    T = logits.shape[0]
+    heavy = np.nonzero(nloc >= 4)[0][: n // 2]
+    rng = np.random.default_rng(seed)
+    rest = rng.choice(T, size=min(T, n), replace=False)
+    rows = np.unique(np.concatenate([heavy, [0, T - 1], rest]))[:n]
+    r = torch.from_numpy(rows).to(x.routing_logits.device)
+    xs = replace(x, routing_logits=x.routing_logits[r], hidden_states=x.hidden_states[r],
+                 hidden_states_scale=x.hidden_states_scale[:, r].contiguous())
+    return rows, xs

@@ -18,7 +18,7 @@ def deterministic(pkg):
 
 @pytest.mark.parametrize("T,skewed", [(64, False), (600, True)])
 def test_repeated_calls_are_bit_identical(T, skewed, pkg, oracle, deterministic):
-    x = pkg.inputs.make_inputs(T, seed=5, device="cuda", skewed=skewed, weight_experts=8)
+    x = pkg.inputs.make_inputs(T, seed=5, device="cuda", skewed=skewed)
     outs = [pkg.run(*x.args()).clone() for _ in range(3)]
     torch.cuda.synchronize()
     assert pkg.read_device_error() == 0

@@ -7,6 +7,7 @@ import importlib.util
 import json
 import pathlib
 
+import numpy as np
 import pytest
 import torch
 
@@ -64,7 +65,7 @@ def test_binding_loads_and_rejects_host_tensors():
 @pytest.mark.gpu
 def test_binding_matches_library_call(pkg, oracle):
     run = _binding()
-    x = pkg.inputs.make_inputs(17, seed=23, device="cuda", weight_experts=8)
+    x = pkg.inputs.make_inputs(17, seed=23, device="cuda")
     out = torch.empty(17, 7168, dtype=torch.bfloat16, device="cuda")
     a = x.args()
     run(a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], int(a[8]), float(a[9]), out)
@@ -74,6 +75,10 @@ def test_binding_matches_library_call(pkg, oracle):
     torch.cuda.synchronize()
     # same kernels; the fp32 combine adds in a run-dependent order, so compare with the parity bar
     assert torch.allclose(out.float(), ref.float(), atol=1e-2, rtol=2e-2)
+    # and with the CPU oracle, like every other entry point
+    o = oracle.moe_forward(*a)
+    err = np.abs(out.float().cpu().numpy() - o)
+    assert (err <= 1e-2 + 2e-2 * np.abs(o)).all(), f"max abs err {err.max():.3e}"
     with pytest.raises(ValueError):
         bad = _args(17, "cuda", E=8)
         bad[3] = torch.zeros(17, 56, device="cuda")              # scale layout must be [56, T]

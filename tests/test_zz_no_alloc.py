@@ -7,8 +7,10 @@ reserved), so they cannot hand over the workspace the other entry points take.
 Its scratch lives in a fixed array inside the library. This test calls it
 through the C ABI twice in a row, on two different inputs, and checks each
 result against the workspace-based moe_fp8_route: ids identical, weights within
-the routing tolerance used elsewhere (rtol 1e-6). It also checks that a token
-count above the array's limit is rejected.
+the routing tolerance used elsewhere (rtol 1e-6). The first call is also
+checked directly against the reference's own routing of the same tokens (the
+golden vectors made by running the operator definition's reference). It also
+checks that a token count above the array's limit is rejected.
 """
 import ctypes
 
@@ -17,6 +19,7 @@ import pytest
 import torch
 
 from cases import routing_case
+from conftest import load_golden, same_selection
 
 pytestmark = pytest.mark.gpu
 
@@ -52,6 +55,16 @@ def test_static_routing_matches_workspace_routing_twice(pkg):
         idx, w = _route_static(pkg, logits, bias, offset, E)
         assert (idx == ref_idx).all(), f"{name}: expert ids differ"
         np.testing.assert_allclose(w, ref_w, rtol=1e-6, atol=1e-7)
+        if name == "routing_T4096_seed12_skewed":
+            g = load_golden(name)
+            s = 1.0 / (1.0 + np.exp(-logits.cpu().numpy().astype(np.float32)))
+            sb = (s + bias.float().cpu().numpy()[None]).astype(np.float32)
+            same = same_selection(idx, g["topk_idx"].astype(np.int64), sb)
+            assert same.all(), f"{(~same).sum()} tokens select a different set than the reference"
+            exact = (np.sort(idx, 1) == g["topk_idx"]).all(1)
+            p = np.argsort(idx, 1)
+            np.testing.assert_allclose(np.take_along_axis(w, p, 1)[exact], g["topk_weights"][exact],
+                                       rtol=1e-6, atol=1e-7)
 
 
 def test_static_routing_rejects_too_many_tokens(pkg):
