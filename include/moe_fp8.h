@@ -67,6 +67,18 @@ int moe_fp8_block_scale_run(const MoeFp8Args* args, void* stream);
  * reference's stages are the separate launches of solution/cuda/pure_moe.cu:589-661. */
 int moe_fp8_run_stage(const MoeFp8Args* args, int32_t stage, void* stream);
 
+/* The operator with the routing already made (expert parallelism: the rows a
+ * rank received from other ranks, with the selections their sources made):
+ * topk_idx / topk_weights [T, 8] replace routing_logits and routing_bias, which
+ * may be NULL (an id outside [0, 256) selects nothing). With args->output
+ * NULL the rounding pass is skipped: each row that has a local expert keeps
+ * its fp32 result in the workspace's combine accumulator (moe_fp8_ep_peer_return
+ * reads it there); not available in deterministic mode. Follows the expert
+ * loop of the definition's reference (...json:146, step 3) for given
+ * selections. */
+int moe_fp8_block_scale_run_routed(const MoeFp8Args* args, const int32_t* topk_idx, const float* topk_weights,
+                                   void* stream);
+
 /* GEMM kernel family used for a call with `num_tokens` tokens:
  *   0  128-row tile kernels for both GEMMs (prefill shapes),
  *   1  weight-streaming GEMM1 + tile GEMM2,
@@ -130,7 +142,7 @@ int moe_fp8_read_device_error(void* workspace, void* stream, int32_t* bits);
 
 /* Test hook for the bounded waits (affects every later launch in this process
  * on the current device): `wait_limit_ns` replaces the 2 s limit of every
- * device-side wait, and `gate_extra` is added to the target of the streaming
+ * device-side wait (the expert-parallel flag waits included), and `gate_extra` is added to the target of the streaming
  * kernel's GEMM2 gate (the count of finished GEMM1 tiles it waits for), so a
  * test can make that wait run out without faulting anything. Restore with
  * (2000000000, 0). Returns MOE_OK or MOE_ERR_INVALID_ARGUMENT / MOE_ERR_CUDA.
@@ -188,6 +200,55 @@ int moe_fp8_ep_pack(const float* routing_logits, const void* hidden_states, cons
 int moe_fp8_ep_scales(const float* token_major_scales, int32_t num_tokens, float* hidden_states_scale, void* stream);
 int moe_fp8_ep_combine(const void* returned_partials, const int32_t* slot, const int32_t* send_offsets,
                        int32_t wave_tokens, int32_t num_tokens, int32_t world, void* output, void* stream);
+
+/* ---- Expert parallelism over peer memory (one GPU per rank, W <= 8 ranks on
+ * one NVLink/NVSwitch node, 256 % W == 0). No host synchronisation and no
+ * collective library on the data path: each rank owns an exchange buffer that
+ * every peer maps (CUDA IPC), and the kernels move rows with plain peer stores
+ * and publish (epoch) flags; every wait is bounded. One step on rank r, with
+ * `epoch` increased by one per step on every rank and T <= capacity tokens:
+ *   1. moe_fp8_route (E = 256) of the rank's tokens, then
+ *      moe_fp8_ep_peer_dispatch: selections (expert id, weight) of every token
+ *      slot to every rank, FP8 row + 56 scales to the ranks owning one of its
+ *      experts, then flags.
+ *   2. moe_fp8_ep_peer_wait(which = 0), then moe_fp8_block_scale_run_routed on
+ *      the W * capacity received rows (moe_fp8_ep_peer_recv_view) with
+ *      output = NULL and local_expert_offset = r * 256 / W, then
+ *      moe_fp8_ep_peer_return (fp32 rows back to their sources, then flags).
+ *   3. moe_fp8_ep_peer_wait(which = 1), then moe_fp8_ep_peer_combine: each
+ *      token's partials summed in fp32 in ascending rank order, rounded once.
+ * A wait that runs out sets a bit in the buffer's error word (16: dispatch
+ * wait, 32: return wait; moe_fp8_ep_peer_read_error) and the step's combine
+ * writes NaN rows. The reference has no multi-GPU path; its only
+ * expert-parallel hook is local_expert_offset (...json:146). */
+typedef struct MoeFp8EpRecvView {
+  void* hidden_states;          /* e4m3 [W * capacity, 7168], row s * capacity + t */
+  float* hidden_states_scale;   /* f32 [56, W * capacity] */
+  int32_t* topk_idx;            /* [W * capacity, 8] global expert ids, -1 past a source's tokens */
+  float* topk_weights;          /* [W * capacity, 8] */
+  int32_t num_rows;             /* W * capacity */
+} MoeFp8EpRecvView;
+size_t moe_fp8_ep_peer_buffer_bytes(int32_t capacity, int32_t world);
+int moe_fp8_ep_peer_buffer_alloc(int32_t capacity, int32_t world, void** base);
+int moe_fp8_ep_peer_buffer_free(void* base);
+/* 64-byte CUDA IPC handle of a buffer, and its mapping in another process. */
+int moe_fp8_ep_peer_ipc_handle(void* base, void* handle);
+int moe_fp8_ep_peer_ipc_open(const void* handle, void** base);
+int moe_fp8_ep_peer_ipc_close(void* base);
+int moe_fp8_ep_peer_recv_view(void* base, int32_t capacity, int32_t world, MoeFp8EpRecvView* view);
+/* peer_bases: host array of the W ranks' buffer addresses as mapped in this process. */
+int moe_fp8_ep_peer_dispatch(const int32_t* topk_idx, const float* topk_weights, const void* hidden_states,
+                             const float* hidden_states_scale, int32_t num_tokens, int32_t capacity, int32_t rank,
+                             int32_t world, void* const* peer_bases, uint32_t epoch, void* stream);
+/* which = 0: the W dispatch flags, 1: the W return flags of this rank's buffer. */
+int moe_fp8_ep_peer_wait(void* base, int32_t world, int32_t which, uint32_t epoch, void* stream);
+/* workspace: the one moe_fp8_block_scale_run_routed used for the W * capacity received rows. */
+int moe_fp8_ep_peer_return(void* workspace, int32_t num_local_experts, int32_t local_expert_offset,
+                           int32_t capacity, int32_t rank, int32_t world, void* const* peer_bases, uint32_t epoch,
+                           void* stream);
+int moe_fp8_ep_peer_combine(const int32_t* topk_idx, int32_t num_tokens, int32_t capacity, int32_t world,
+                            void* base, void* output, void* stream);
+int moe_fp8_ep_peer_read_error(void* base, void* stream, int32_t* bits);
 
 /* Text of the last error on the calling thread (the reference raises the
  * equivalent message through TVM_FFI_ICHECK, solution/cuda/main.cpp:20-34). */

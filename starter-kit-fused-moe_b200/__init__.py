@@ -69,6 +69,10 @@ EXPORTED_SYMBOLS = (
     "moe_fp8_set_gemm_path", "moe_fp8_gemm_path", "moe_fp8_route_static",
     "moe_fp8_ep_plan", "moe_fp8_ep_pack", "moe_fp8_ep_scales", "moe_fp8_ep_combine",
     "moe_fp8_quantize_activations", "moe_fp8_set_deterministic", "moe_fp8_debug_set_waits",
+    "moe_fp8_block_scale_run_routed", "moe_fp8_ep_peer_buffer_bytes", "moe_fp8_ep_peer_buffer_alloc",
+    "moe_fp8_ep_peer_buffer_free", "moe_fp8_ep_peer_ipc_handle", "moe_fp8_ep_peer_ipc_open",
+    "moe_fp8_ep_peer_ipc_close", "moe_fp8_ep_peer_recv_view", "moe_fp8_ep_peer_dispatch", "moe_fp8_ep_peer_wait",
+    "moe_fp8_ep_peer_return", "moe_fp8_ep_peer_combine", "moe_fp8_ep_peer_read_error",
 )
 
 _lib = None

@@ -171,6 +171,9 @@ struct Plan {
   int path;  // see gemm_path()
   bool det;  // deterministic combine (see moe_fp8_set_deterministic)
   float* pair_out;
+  const int* given_idx;    // routed mode: selections made elsewhere [T, 8]
+  const float* given_w;
+  bool f32_out;            // routed mode without output: fp32 rows stay in the workspace
 };
 
 // GEMM kernel families per call:
@@ -204,18 +207,25 @@ int gemm_path(int T) {
   return T <= 240 ? 2 : 0;
 }
 
-int make_plan(const MoeFp8Args* a, Plan& p) {
+int make_plan(const MoeFp8Args* a, Plan& p, const int* given_idx = nullptr, const float* given_w = nullptr) {
   if (!a) return fail(MOE_ERR_INVALID_ARGUMENT, "args is NULL");
   const int T = a->num_tokens, E = a->num_local_experts;
   if (T < 0) return fail(MOE_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
   if (E < 1 || E > moe::kMaxLocalExperts)
     return fail(MOE_ERR_INVALID_ARGUMENT, "num_local_experts must be in [1, 256]");
   if (T == 0) return MOE_OK;
-  if (!a->routing_logits || !a->hidden_states || !a->hidden_states_scale || !a->gemm1_weights ||
-      !a->gemm1_weights_scale || !a->gemm2_weights || !a->gemm2_weights_scale || !a->output)
+  const bool routed = given_idx != nullptr;
+  if (routed && !given_w) return fail(MOE_ERR_INVALID_ARGUMENT, "topk_weights is NULL");
+  if ((!routed && !a->routing_logits) || !a->hidden_states || !a->hidden_states_scale || !a->gemm1_weights ||
+      !a->gemm1_weights_scale || !a->gemm2_weights || !a->gemm2_weights_scale || (!routed && !a->output))
     return fail(MOE_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
-  if (!aligned(a->routing_logits, 16) || !aligned(a->hidden_states, 16) || !aligned(a->gemm1_weights, 16) ||
-      !aligned(a->gemm2_weights, 16) || !aligned(a->output, 16) ||
+  if (routed && !a->output && deterministic())
+    return fail(MOE_ERR_INVALID_ARGUMENT, "fp32 routed output is not available in deterministic mode");
+  p.given_idx = given_idx;
+  p.given_w = given_w;
+  p.f32_out = routed && !a->output;
+  if ((!routed && !aligned(a->routing_logits, 16)) || !aligned(a->hidden_states, 16) ||
+      !aligned(a->gemm1_weights, 16) || !aligned(a->gemm2_weights, 16) || !aligned(a->output, 16) ||
       (a->routing_bias && !aligned(a->routing_bias, 16)) || !aligned(a->hidden_states_scale, 16) ||
       !aligned(a->gemm1_weights_scale, 16) || !aligned(a->gemm2_weights_scale, 16))
     return fail(MOE_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
@@ -265,7 +275,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       e = moe::launch_route(a->routing_logits, static_cast<const __nv_bfloat16*>(a->routing_bias), T,
                             a->local_expert_offset, E, a->routed_scaling_factor, p.topk_idx, p.topk_w, p.pair_pos,
                             p.counts, (p.path >= 2 || p.det) ? nullptr : p.acc, static_cast<__nv_bfloat16*>(a->output),
-                            st);
+                            st, p.given_idx, p.given_w);
       if (e != cudaSuccess) return cuda_fail(e, "routing kernel launch");
       break;
     case 1:
@@ -354,6 +364,7 @@ int launch_stage(const Plan& p, int stage, cudaStream_t st) {
       break;
     }
     case 4:
+      if (p.f32_out) break;      // routed mode without output: the fp32 rows stay in the workspace
       if (p.det) {
         e = moe::launch_finalize_ordered(p.pair_out, static_cast<__nv_bfloat16*>(a->output), T, p.topk_idx, p.pair_pos,
                                          p.counts, a->local_expert_offset, E, p.err, st);
@@ -377,6 +388,18 @@ extern "C" {
 int moe_fp8_block_scale_run(const MoeFp8Args* a, void* stream) {
   Plan p{};
   if (int rc = make_plan(a, p)) return rc;
+  if (a->num_tokens == 0) return MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int stage = 0; stage < 5; ++stage)
+    if (int rc = launch_stage(p, stage, st)) return rc;
+  return MOE_OK;
+}
+
+int moe_fp8_block_scale_run_routed(const MoeFp8Args* a, const int32_t* topk_idx, const float* topk_weights,
+                                   void* stream) {
+  if (!topk_idx) return fail(MOE_ERR_INVALID_ARGUMENT, "topk_idx is NULL");
+  Plan p{};
+  if (int rc = make_plan(a, p, topk_idx, topk_weights)) return rc;
   if (a->num_tokens == 0) return MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int stage = 0; stage < 5; ++stage)
@@ -456,6 +479,7 @@ int moe_fp8_debug_set_waits(uint64_t wait_limit_ns, int32_t gate_extra) {
   if (wait_limit_ns == 0 || gate_extra < 0) return fail(MOE_ERR_INVALID_ARGUMENT, "debug_set_waits: bad arguments");
   cudaError_t e = moe::set_debug_waits_stream(wait_limit_ns, gate_extra);
   if (e == cudaSuccess) e = moe::set_debug_waits_tile(wait_limit_ns, gate_extra);
+  if (e == cudaSuccess) e = moe::set_debug_waits_ep(wait_limit_ns, gate_extra);
   return e == cudaSuccess ? MOE_OK : cuda_fail(e, "debug_set_waits");
 }
 

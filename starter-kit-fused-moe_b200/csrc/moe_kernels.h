@@ -28,7 +28,8 @@ struct GemmArgs {
 
 cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
                          int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
-                         __nv_bfloat16* out, cudaStream_t st);
+                         __nv_bfloat16* out, cudaStream_t st, const int* given_idx = nullptr,
+                         const float* given_w = nullptr);
 cudaError_t launch_permute(const uint8_t* hidden, const float* hs, int T, int E, int offset, const int* topk_idx,
                            const float* topk_w, const int* pair_pos, const int* counts, int R1, uint8_t* a1,
                            float* sa1, int* row_token, float* row_weight, int* err, int num_sms, cudaStream_t st);
@@ -77,6 +78,7 @@ cudaError_t launch_quantize(const void* x, bool bf16, int T, uint8_t* q, float* 
 // Test hooks of the bounded waits (one per translation unit with waits).
 cudaError_t set_debug_waits_stream(unsigned long long limit_ns, int gate_extra);
 cudaError_t set_debug_waits_tile(unsigned long long limit_ns, int gate_extra);
+cudaError_t set_debug_waits_ep(unsigned long long limit_ns, int gate_extra);
 // Text returned by moe_fp8_last_error() on the calling thread.
 void set_last_error(const char* msg);
 cudaError_t set_trace(int on);

@@ -32,10 +32,15 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 // Local selections are counted per block in shared memory and published with
 // one global atomic per (block, expert); each selection gets its position
 // inside its expert's group (pair_pos), -1 when the expert is not local.
+// With `given_idx` set, the selections are not computed: token t's 8 experts
+// and weights are read from given_idx / given_w [T, 8] (an id outside
+// [0, 256) selects nothing) and only the bookkeeping below runs; this is how a
+// rank runs the experts of tokens that other ranks routed.
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
     const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, int T, int offset, int E,
     float scale, int* __restrict__ topk_idx, float* __restrict__ topk_w, int* __restrict__ pair_pos,
-    int* __restrict__ counts, float* __restrict__ out_acc, __nv_bfloat16* __restrict__ out) {
+    int* __restrict__ counts, float* __restrict__ out_acc, __nv_bfloat16* __restrict__ out,
+    const int* __restrict__ given_idx, const float* __restrict__ given_w) {
   __shared__ int hist[kMaxLocalExperts];
   __shared__ int base[kMaxLocalExperts];
   pdl_trigger();
@@ -45,7 +50,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
   const bool active = t < T;  // warp-uniform
   float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
   uint4 braw = make_uint4(0, 0, 0, 0);
-  if (active) {
+  if (active && given_idx == nullptr) {
     const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExperts + lane * 8);
     x0 = __ldg(lp);
     x1 = __ldg(lp + 1);
@@ -53,7 +58,25 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
   }
   __syncthreads();
   int my_le = -1, my_lpos = 0;
-  if (active) {
+  if (active && given_idx != nullptr) {
+    if (lane < kTopK) {
+      const int sel = __ldg(given_idx + (size_t)t * kTopK + lane);
+      const float w = __ldg(given_w + (size_t)t * kTopK + lane);
+      topk_idx[(size_t)t * kTopK + lane] = sel;
+      topk_w[(size_t)t * kTopK + lane] = w;
+      const int le = sel - offset;
+      if (sel >= 0 && sel < kExperts && le >= 0 && le < E) {
+        my_le = le;
+        my_lpos = atomicAdd(&hist[le], 1);
+      }
+    }
+    if (__ballot_sync(0xffffffffu, my_le >= 0) != 0 && out_acc != nullptr) {
+      float4* row = reinterpret_cast<float4*>(out_acc + (size_t)t * kHidden);
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int c = lane; c < kHidden / 4; c += 32) row[c] = z;
+    }
+  } else if (active) {
     const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
     const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&braw);
     float s[8], sb[8];
@@ -335,11 +358,11 @@ __global__ void __launch_bounds__(256) finalize_ordered_kernel(const float* __re
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_route(const float* logits, const __nv_bfloat16* bias, int T, int offset, int E, float scale,
                          int* topk_idx, float* topk_w, int* pair_pos, int* counts, float* out_acc,
-                         __nv_bfloat16* out, cudaStream_t st) {
+                         __nv_bfloat16* out, cudaStream_t st, const int* given_idx, const float* given_w) {
   if (T == 0) return cudaSuccess;
   const int grid = (T + kRouteWarps - 1) / kRouteWarps;
   route_kernel<<<grid, kRouteWarps * 32, 0, st>>>(logits, bias, T, offset, E, scale, topk_idx, topk_w, pair_pos,
-                                                  counts, out_acc, out);
+                                                  counts, out_acc, out, given_idx, given_w);
   return cudaGetLastError();
 }
 

@@ -1,6 +1,6 @@
-"""GPU, 2+ devices: expert-parallel forward over NCCL equals the single-GPU
-256-expert operator (tests/ep_gpu_check.py under torchrun). Skipped when the
-machine has fewer than two GPUs."""
+"""GPU, 2+ devices: expert-parallel forward (peer-memory and collective
+transports) against the CPU oracle over all 256 experts (tests/ep_gpu_check.py
+under torchrun, NVLS off). Skipped when the machine has fewer than two GPUs."""
 import os
 import subprocess
 import sys
