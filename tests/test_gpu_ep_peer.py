@@ -24,7 +24,7 @@ from conftest import assert_close
 pytestmark = pytest.mark.gpu
 
 POOL = 72
-CAPACITY = 64
+CAPACITY = 72
 
 
 @pytest.fixture(scope="module")
