@@ -471,6 +471,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--skewed", action="store_true", help="BASELINE config 3 routing bias (+3 on 4 local experts)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -492,7 +493,7 @@ def main():
     pkg = ge.load_package()
     hbm_peak, bf16_peak, peak_kind = load_peaks()
     T = a.tokens
-    x = pkg.inputs.make_inputs(T, seed=rank, device="cuda")
+    x = pkg.inputs.make_inputs(T, seed=rank, device="cuda", skewed=a.skewed)
     op = Op(pkg, x)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     for _ in range(a.warmup):
@@ -557,7 +558,7 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)",
         "data": "synthetic (seeded, benchmark distributions; random-init weights)",
         "config": {"workload": f"{'decode' if pkg.gemm_path(T) == 2 else 'prefill'} T={T} tokens per GPU, "
-                               "E_local=32, local_expert_offset=0",
+                               f"E_local=32, local_expert_offset=0{', skewed bias' if a.skewed else ''}",
                    "tokens": T, "local_experts": 32, "pairs": pairs, "hit_experts": hit,
                    "parallelism": "replicas" if world > 1 else "single",
                    "l2": "flushed (256 MB write) between timed calls; weights also exceed L2"},
