@@ -9,7 +9,8 @@ the same seeded inputs and a destination-passing output; each is timed with
 CUDA events after 3 warm-up calls, L2 flushed (256 MB write) before every timed
 call, median of 10, and the two outputs are compared. One JSON line per token
 count. A measurement aid only: nothing in the operator imports it. The
-reference's CuTe GEMM uses cluster TMA multicast, so run this on one GPU only.
+reference's CuTe GEMM shares operand tiles across a thread-block cluster, so
+run this on one GPU only, never inside a multi-GPU job.
 """
 from __future__ import annotations
 
