@@ -425,7 +425,7 @@ GEMM1_FLOPS_PER_PAIR = 2 * H * 2 * I
 GEMM2_FLOPS_PER_PAIR = 2 * I * H
 
 
-def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, fp8_peak, n=5, warm=3, E=32):
+def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, n=5, warm=3, E=32):
     """One operator call configuration: whole-call time, per-GEMM stage-alone
     times, and each against its roofline t_bound = max(bytes / HBM peak,
     useful FLOPs / FP8 peak) (frac = t_bound / t)."""
@@ -440,15 +440,8 @@ def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, fp8_peak, n=5, warm=3, E=
     g2 = statistics.median(timed(lambda: op.stage(3), n, flush)) if path != 2 else 0.0
     b = algorithmic_bytes(T, pairs, hit)
     fl = pairs * FLOPS_PER_PAIR
-    hbm = hbm_peak * 1e9
-    fp8 = fp8_peak * 1e12
-
     def roof(bytes_, flops, ms):
-        tb = max(bytes_ / hbm, flops / fp8)
-        return {"us": ms * 1e3, "bytes": bytes_, "useful_flops": flops, "t_bound_us": tb * 1e6,
-                "bound": "hbm" if bytes_ / hbm >= flops / fp8 else "tensor",
-                "frac": tb / (ms * 1e-3), "tflops": flops / (ms * 1e-3) / 1e12,
-                "tensor_frac_of_fp8_peak": flops / (ms * 1e-3) / fp8}
+        return {"us": ms * 1e3, "bytes": bytes_, "useful_flops": flops, "tflops": flops / (ms * 1e-3) / 1e12}
 
     res = {"T": T, "skewed": skewed, "local_experts": E, "us_per_call": t * 1e3, "pairs": pairs, "hit_experts": hit,
            "tflops": fl / (t * 1e-3) / 1e12, "hbm_gbs": b / (t * 1e-3) / 1e9,
@@ -463,6 +456,19 @@ def sweep_point(pkg, T, skewed, seed, flush, hbm_peak, fp8_peak, n=5, warm=3, E=
     del op, x
     torch.cuda.empty_cache()
     return res
+
+
+def add_rooflines(point, hbm_peak, fp8_peak):
+    """Fill in each kernel entry of a sweep point: t_bound = max(bytes / HBM peak,
+    useful FLOPs / FP8 peak), frac = t_bound / t, and the tensor fraction."""
+    hbm, fp8 = hbm_peak * 1e9, fp8_peak * 1e12
+    for k, v in point.items():
+        if isinstance(v, dict) and "useful_flops" in v:
+            tb = max(v["bytes"] / hbm, v["useful_flops"] / fp8)
+            t = v["us"] * 1e-6
+            v.update({"t_bound_us": tb * 1e6, "bound": "hbm" if v["bytes"] / hbm >= v["useful_flops"] / fp8 else "tensor",
+                      "frac": tb / t, "tensor_frac_of_fp8_peak": v["useful_flops"] / t / fp8})
+    return point
 
 
 def main():
@@ -548,9 +554,6 @@ def main():
     e2e_ms = max_over_ranks(sum(e2e_times), world) / a.steps
     h2d = h_in.numel()
     d2h = h_out.numel() * h_out.element_size()
-    # the FP8 peak is measured after the timed regions (its seconds of dense GEMM
-    # would leave the power limiter engaged for the decode calls)
-    fp8_burst, fp8_sustained = measure_fp8_peak()
 
     line = {
         "metric": "fused_moe_us_per_call", "value": ms_per_step * 1e3, "unit": "us", "n_gpus": world,
@@ -569,9 +572,7 @@ def main():
                      "frac": g1_achieved / hbm_peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": g1_bytes, "launch_us": g1_ms * 1e3,
                      "traffic": STREAM_TRAFFIC_BYTES_T64 if (T == 64 and path == 2) else None},
-        "peaks": {"hbm_gbs": hbm_peak, "hbm_kind": peak_kind, "fp8_tflops_burst": fp8_burst,
-                  "fp8_tflops_sustained": fp8_sustained,
-                  "fp8_how": "measured in this run: torch._scaled_mm e4m3 8192^3 (cuBLASLt), best of 10 / 2 s loop"},
+
         "e2e": {"value": e2e_ms * 1e3, "unit": "us", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": a.steps * int(pkg.load_library().moe_fp8_kernels_per_call(T)),
         "clocks": clk.summary(),
@@ -584,8 +585,17 @@ def main():
         # prefill points use the FP8 burst peak (each kernel is timed alone, milliseconds long)
         for (tt, sk, e) in ((1, False, 32), (8, False, 32), (32, False, 32), (4096, False, 32), (16384, True, 32),
                             (8192, False, 256)):
-            sw.append(sweep_point(pkg, tt, sk, 0 if e == 32 else 100, flush, hbm_peak, fp8_burst, E=e))
+            sw.append(sweep_point(pkg, tt, sk, 0 if e == 32 else 100, flush, hbm_peak, E=e))
         line["sweep"] = sw
+    # the FP8 peak is measured after every timed region: its seconds of dense GEMM
+    # leave the power limiter engaged for a while
+    fp8_burst, fp8_sustained = measure_fp8_peak()
+    line["peaks"] = {"hbm_gbs": hbm_peak, "hbm_kind": peak_kind, "fp8_tflops_burst": fp8_burst,
+                     "fp8_tflops_sustained": fp8_sustained,
+                     "fp8_how": "measured in this run after the timed regions: torch._scaled_mm e4m3 8192^3 "
+                                "(cuBLASLt), best of 10 / 2 s loop"}
+    for p in line.get("sweep", []):
+        add_rooflines(p, hbm_peak, fp8_burst)
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         O = ge.load_oracle()
         dt = cpu_reference_time(O, x)
