@@ -84,3 +84,51 @@ def test_deterministic_switch_and_workspace(pkg):
     finally:
         pkg.set_deterministic(old)
     assert lib.moe_fp8_workspace_bytes(64, 32) == base
+
+
+def test_routed_run_argument_checks(pkg):
+    """moe_fp8_block_scale_run_routed rejects missing selections and the fp32
+    routed output in deterministic mode before launching anything."""
+    lib = pkg.load_library()
+    f = lib.moe_fp8_block_scale_run_routed
+    f.argtypes = [ctypes.POINTER(pkg.MoeFp8Args), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    a = pkg.MoeFp8Args()
+    a.num_tokens, a.num_local_experts = 4, 32
+    assert f(ctypes.byref(a), None, None, None) == 1
+    assert b"topk_idx" in lib.moe_fp8_last_error()
+    fake = ctypes.c_void_p(256)                      # never dereferenced: the checks fail first
+    assert f(ctypes.byref(a), fake, None, None) == 1
+    assert b"topk_weights" in lib.moe_fp8_last_error()
+    a.hidden_states = a.hidden_states_scale = a.gemm1_weights = a.gemm1_weights_scale = 256
+    a.gemm2_weights = a.gemm2_weights_scale = 256
+    old = pkg.set_deterministic(True)
+    try:
+        assert f(ctypes.byref(a), fake, fake, None) == 1
+        assert b"deterministic" in lib.moe_fp8_last_error()
+    finally:
+        pkg.set_deterministic(old)
+    a.num_tokens = 0
+    assert f(ctypes.byref(a), fake, fake, None) == 0     # T = 0 is a no-op
+
+
+def test_peer_exchange_geometry_checks(pkg):
+    """Exchange-buffer sizes and the argument checks of the peer-memory entries
+    (no device memory is touched)."""
+    lib = pkg.load_library()
+    nb = lib.moe_fp8_ep_peer_buffer_bytes
+    nb.argtypes, nb.restype = [ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t
+    assert nb(0, 2) == 0 and nb(16, 0) == 0 and nb(16, 9) == 0      # W <= 8
+    b2, b8 = nb(8192, 2), nb(8192, 8)
+    # rows of 7168 FP8 bytes + 56 scales + 8 ids + 8 weights, and fp32 return rows, per (source, slot)
+    per_row = 7168 + 56 * 4 + 8 * 4 + 8 * 4 + 7168 * 4
+    assert b2 >= 2 * 8192 * per_row and b8 >= 8 * 8192 * per_row and b8 < 8 * 8192 * per_row + 2 ** 20
+    d = lib.moe_fp8_ep_peer_dispatch
+    d.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int32] * 4 + [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
+    peers = (ctypes.c_void_p * 2)(1024, 2048)
+    assert d(None, None, None, None, 9, 8, 0, 2, peers, 1, None) == 1           # T > capacity
+    assert d(None, None, None, None, 4, 8, 0, 3, peers, 1, None) == 1           # 256 % 3 != 0
+    assert d(None, None, None, None, 4, 8, 2, 2, peers, 1, None) == 1           # rank >= world
+    assert d(None, None, None, None, 4, 8, 0, 2, peers, 1, None) == 1           # NULL token tensors
+    w = lib.moe_fp8_ep_peer_wait
+    w.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p]
+    assert w(None, 2, 0, 1, None) == 1 and w(ctypes.c_void_p(1024), 2, 2, 1, None) == 1
