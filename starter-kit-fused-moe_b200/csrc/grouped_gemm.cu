@@ -36,6 +36,7 @@
 //          reductions (cp.reduce.async.bulk .add.f32), so the top-k combine
 //          happens here, with no separate reduce pass, and overlaps the next
 //          tile's main loop.
+#include <cstdio>
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 #include "moe_workspace.h"
@@ -133,16 +134,99 @@ struct GemmCfg<2> {
   static constexpr int STAGING = EPI_WARPS * 16 * ROW_STRIDE;
 };
 
-template <int MODE>
+// CTA pairs (PAIR): a cluster of two CTAs computes a 256-row tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256), issued by the leader (cluster rank
+// 0). Each CTA loads its own 128 A rows and half of B (128 rows, N split across
+// the pair) and keeps its 128 rows x 256 columns of every K-block's partial in
+// its own TMEM, so promotion and epilogue are the single-CTA ones. A stage is
+// 32 KB per CTA instead of 48 KB: the operand ingest per SM, the pace-setter of
+// the single-CTA kernels, drops by a third and more stages fit.
+template <int MODE, bool PAIR>
 constexpr int stage_bytes() {
-  return (BM + BN) * GemmCfg<MODE>::SK;
+  return (BM + (PAIR ? BN / 2 : BN)) * GemmCfg<MODE>::SK;
 }
-template <int MODE>
+template <int MODE, bool PAIR>
+constexpr int num_stages() {
+  return PAIR ? (MODE == 1 ? 5 : 4) : GemmCfg<MODE>::STAGES;
+}
+template <int MODE, bool PAIR>
 constexpr size_t gemm_smem_bytes() {
-  return 1024 + (size_t)GemmCfg<MODE>::STAGES * stage_bytes<MODE>() + GemmCfg<MODE>::STAGING + sizeof(GemmSmem);
+  return 1024 + (size_t)num_stages<MODE, PAIR>() * stage_bytes<MODE, PAIR>() + GemmCfg<MODE>::STAGING +
+         sizeof(GemmSmem);
 }
-static_assert(gemm_smem_bytes<1>() <= 232448 && gemm_smem_bytes<2>() <= 232448, "shared memory budget");
+static_assert(gemm_smem_bytes<1, false>() <= 232448 && gemm_smem_bytes<2, false>() <= 232448, "shared memory budget");
+static_assert(gemm_smem_bytes<1, true>() <= 232448 && gemm_smem_bytes<2, true>() <= 232448, "shared memory budget");
+static_assert(num_stages<1, true>() <= MAX_STAGES && num_stages<2, true>() <= MAX_STAGES, "barrier arrays");
 static_assert(GemmCfg<1>::STAGES <= MAX_STAGES && GemmCfg<2>::STAGES <= MAX_STAGES, "barrier arrays");
+static_assert(GemmCfg<1>::SK == 128 && GemmCfg<2>::SK == 128, "the CTA-pair tiles assume 128-wide stages");
+
+// ---- cluster / CTA-pair primitives
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier of either CTA of the pair (cluster address). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mma_e4m3_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives once on the mbarrier at this offset in both CTAs of the pair when the
+// leader's issued tcgen05 operations are done.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   bar), "h"((uint16_t)3)
+               : "memory");
+}
+// Bounded wait with cluster-scope acquire (for a barrier the other CTA of the pair arrives on).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
+  auto try_wait = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_wait()) return true;
+  const unsigned long long t0 = globaltimer_ns(), limit = g_wait_limit_ns;
+  while (true) {
+    if (try_wait()) return true;
+    if (globaltimer_ns() - t0 > limit) return false;
+  }
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
 static_assert((GemmCfg<1>::SK == 128 || GemmCfg<1>::SK == 64) && (GemmCfg<2>::SK == 128 || GemmCfg<2>::SK == 64),
               "stage K width");
 
@@ -237,13 +321,18 @@ __device__ __forceinline__ float2 unpack_e4m3x2(uint32_t v16) {
   return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
-template <int MODE>
+template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmOut, GemmArgs args) {
   using Cfg = GemmCfg<MODE>;
-  constexpr int KB = Cfg::KB, NT = Cfg::NT, STAGES = Cfg::STAGES, SK = Cfg::SK, HS = BK / SK;
-  constexpr int A_TILE = BM * SK, B_TILE = BN * SK, STAGE_BYTES = A_TILE + B_TILE;
+  constexpr int KB = Cfg::KB, NT = Cfg::NT, STAGES = num_stages<MODE, PAIR>(), SK = Cfg::SK, HS = BK / SK;
+  constexpr int A_TILE = BM * SK, B_TILE = (PAIR ? BN / 2 : BN) * SK, STAGE_BYTES = A_TILE + B_TILE;
+  constexpr int RB = PAIR ? 2 * BM : BM;   // rows of a tile
+  // the pair's rank (0: leader, issues the MMA), the worker index and count (a pair is one worker)
+  const int crank = PAIR ? (int)cluster_rank() : 0;
+  const int wid = PAIR ? (int)cluster_id() : (int)blockIdx.x;
+  const int G = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
@@ -258,7 +347,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&S.tfull[b]), 1);
-      mbar_init(smem_u32(&S.tempty[b]), EPI_WARPS);
+      mbar_init(smem_u32(&S.tempty[b]), PAIR ? 2 * EPI_WARPS : EPI_WARPS);   // both CTAs' epilogues (leader's copy)
       mbar_init(smem_u32(&S.amax_bar[b]), EPI_WARPS);
     }
     for (int w = 0; w < EPI_WARPS; ++w) {
@@ -286,7 +375,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   {
     const int tid = threadIdx.x;
     const int c = (tid < E) ? args.counts[tid] : 0;
-    const int mt = (c * Cfg::ROWS_PER_PAIR + BM - 1) / BM;
+    const int mt = (c * Cfg::ROWS_PER_PAIR + RB - 1) / RB;
     int tot0, tot1;
     const int roff = block_scan_256(align_up(c, 128), S.warp_sums, tot0);
     const int tstart = block_scan_256(mt * NT, S.warp_sums, tot1);
@@ -298,10 +387,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (tid == 0) {
       S.tile_start[E] = tot1;
       S.total_tiles = tot1;
-      const int G = gridDim.x;
       int tail = tot1 % G, sp = 1;
       if (tail > 0) {
-        sp = min(min(G / tail, Cfg::MAX_SPLITS), (int)(WsLayout::kMaxSplitUnits / tail));
+        // a pair's two CTAs keep one partial tile each
+        sp = min(min(G / tail, Cfg::MAX_SPLITS), (int)(WsLayout::kMaxSplitUnits / ((PAIR ? 2 : 1) * tail)));
         if (sp < 2) sp = 1;
       }
       if (sp == 1 || args.no_split) {
@@ -314,11 +403,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&S.tmem_base), TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      // one warp of each CTA of the pair, same warp id and destination offset
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      tmem_alloc(smem_u32(&S.tmem_base), TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();   // the peer's barriers are initialised before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem_base = S.tmem_base;
   const int units = S.units;
@@ -328,11 +426,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok && !aborted(S); u += gridDim.x) {
+      for (int u = wid; u < units && ok && !aborted(S); u += G) {
         const Unit x = unit_of(S, u, KB);
         int e, nt, mt;
         decode_tile<NT>(S, E, x.tile, e, nt, mt);
-        const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
+        const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * RB + BM * crank;
         for (int ks = x.k0 * HS; ks < x.k1 * HS; ++ks, ++it) {
           const int s = it % STAGES, u = it / STAGES;
           if (!mbar_wait(smem_u32(&S.empty[s]), (u & 1) ^ 1)) {
@@ -345,6 +443,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t sb = sa + A_TILE;
           const int x = ks * SK;
+          if constexpr (PAIR) {
+            // both CTAs' loads complete on the leader's full barrier, which expects both
+            const uint32_t fbl = mapa_shared(fb, 0);
+            if (crank == 0) mbar_arrive_expect_tx(fb, 2 * STAGE_BYTES);
+            tma_load_2d_pair(sa, &tmA, fbl, x, arow);
+            if (MODE == 1)   // N split across the pair: leader the 128 gate rows, peer the 128 up rows
+              tma_load_2d_pair(sb, &tmB, fbl, x, e * kGemm1N + crank * kInter + nt * 128);
+            else
+              tma_load_2d_pair(sb, &tmB, fbl, x, e * kHidden + nt * BN + crank * 128);
+            continue;
+          }
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
           tma_load_2d(sa, &tmA, fb, x, arow);
           if (MODE == 1) {
@@ -357,17 +466,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
+    // ------------------------------------------------------------ MMA issuer (the leader, for a pair)
+    if (lane == 0 && crank == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(PAIR ? 2 * BM : BM, BN);
       int it = 0, kt = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok && !aborted(S); u += gridDim.x) {
+      for (int u = wid; u < units && ok && !aborted(S); u += G) {
         const Unit x = unit_of(S, u, KB);
         for (int kb = x.k0; kb < x.k1 && ok; ++kb, ++kt) {
           const int b = kt & 1, v = kt >> 1;
           trace_mark(kt, 3);
-          if (!mbar_wait(smem_u32(&S.tempty[b]), (v & 1) ^ 1)) {
+          if (!(PAIR ? mbar_wait_cluster(smem_u32(&S.tempty[b]), (v & 1) ^ 1)
+                     : mbar_wait(smem_u32(&S.tempty[b]), (v & 1) ^ 1))) {
             set_abort(S, args.err, kErrTimeoutMma);
             ok = false;
             break;
@@ -387,12 +497,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             for (int kk = 0; kk < SK / 32; ++kk) {
               const uint64_t da = SK == 128 ? sdesc_sw128(sa + kk * 32) : sdesc_sw64(sa + kk * 32);
               const uint64_t db = SK == 128 ? sdesc_sw128(sb + kk * 32) : sdesc_sw64(sb + kk * 32);
-              mma_e4m3(d, da, db, idesc, (h | kk) ? 1u : 0u);
+              if constexpr (PAIR) mma_e4m3_pair(d, da, db, idesc, (h | kk) ? 1u : 0u);
+              else mma_e4m3(d, da, db, idesc, (h | kk) ? 1u : 0u);
             }
-            mma_commit(smem_u32(&S.empty[s]));
+            if constexpr (PAIR) mma_commit_pair(smem_u32(&S.empty[s]));   // frees the stage in both CTAs
+            else mma_commit(smem_u32(&S.empty[s]));
           }
           if (!ok) break;
-          mma_commit(smem_u32(&S.tfull[b]));
+          if constexpr (PAIR) mma_commit_pair(smem_u32(&S.tfull[b]));
+          else mma_commit(smem_u32(&S.tfull[b]));
           trace_mark(kt, 4);
         }
       }
@@ -406,11 +519,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const size_t ld_sa = (size_t)Cfg::ROWS_PER_PAIR * args.R1;
     int kq = 0, j = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok && !aborted(S); u += gridDim.x, ++j) {
+    for (int u = wid; u < units && ok && !aborted(S); u += G, ++j) {
       const Unit x = unit_of(S, u, KB);
       int e, nt, mt;
       decode_tile<NT>(S, E, x.tile, e, nt, mt);
-      const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * BM;
+      const int arow = Cfg::ROWS_PER_PAIR * S.row_off[e] + mt * RB + BM * crank;
       const int tb = j & 1;
       if (!mbar_wait(smem_u32(&S.tbempty[tb]), ((j >> 1) & 1) ^ 1)) {
         set_abort(S, args.err, kErrTimeoutProducer);
@@ -426,7 +539,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       } else {
         // 8 chunks of weight scales, 16 of tokens, 16 of weights
-        const size_t p0 = (size_t)S.row_off[e] + mt * (BM / 2);     // the tile's first pair
+        const size_t p0 = (size_t)S.row_off[e] + (mt * RB + BM * crank) / 2;     // this CTA's first pair
         for (int c = lane; c < 40; c += 32) {
           if (c < 8) cp_async16(smem_u32(buf + 4 * c), args.sb + ((size_t)e * kHiddenBlocks + 2 * nt) * kInterBlocks + 4 * c);
           else if (c < 24) cp_async16(smem_u32(buf + 64 + 4 * (c - 8)), args.row_token + p0 + 4 * (c - 8));
@@ -464,7 +577,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // one 512-byte row each), so the epilogue never waits on the memory system.
     if constexpr (MODE == 2) {
       int j = 0;
-      for (int u = blockIdx.x; u < units && !aborted(S); u += gridDim.x, ++j) {
+      for (int u = wid; u < units && !aborted(S); u += G, ++j) {
         const Unit x = unit_of(S, u, KB);
         int e, nt, mt;
         decode_tile<NT>(S, E, x.tile, e, nt, mt);
@@ -481,7 +594,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (args.pair_out != nullptr) {
               // deterministic mode: the pair's own row (staged row `lane` of epilogue
               // warp w is pair 16 * quadrant + lane of the tile), written once
-              const size_t prow = (size_t)S.row_off[e] + mt * (BM / 2) + 16 * ((w + 2) & 3) + lane;
+              const size_t prow = (size_t)S.row_off[e] + (mt * RB + BM * crank) / 2 + 16 * ((w + 2) & 3) + lane;
               bulk_store(args.pair_out + prow * kHidden + nt * BN + 128 * (w >> 2), smem_u32(row), 128 * sizeof(float));
             } else {
               float* dst = args.out_acc + (size_t)tok * kHidden + nt * BN + 128 * (w >> 2);
@@ -505,7 +618,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int r = 32 * q + lane;     // row inside the tile
     const uint32_t lane_addr = tmem_base + ((uint32_t)(32 * q) << 16);
     int kt = 0, tile_iter = 0, amax_iter = 0;
-    for (int u = blockIdx.x; u < units && !aborted(S); u += gridDim.x, ++tile_iter) {
+    for (int u = wid; u < units && !aborted(S); u += G, ++tile_iter) {
       // the scale loader publishes the decoded tile with the tile's scales
       const int tb = tile_iter & 1;
       const float* tbuf = S.tile_buf[tb];
@@ -557,7 +670,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive(smem_u32(&S.tempty[b]));
+            if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&S.tempty[b]), 0));   // the leader's MMA waits
+            else mbar_arrive(smem_u32(&S.tempty[b]));
             mbar_arrive(smem_u32(&S.scempty[ss]));
           }
           if (warp == 4 && lane == 0) trace_mark(kt, 2);
@@ -572,8 +686,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int e = S.tile_info[tb][0], nt = S.tile_info[tb][1], mt = S.tile_info[tb][2];
       const int row_off_e = S.tile_info[tb][3];
       const int slot = S.tile_info[tb][6], tail_i = S.tile_info[tb][7];
-      const int row_in_expert = mt * BM + r;                  // GEMM row inside the expert's group
+      const int row_in_expert = mt * RB + BM * crank + r;     // GEMM row inside the expert's group
       const bool valid = row_in_expert < Cfg::ROWS_PER_PAIR * S.cnt[e];
+      // a pair tile's second half can start past the expert's 128-row padded group
+      // (GEMM1 groups are 128-aligned; GEMM2 term groups are 256-aligned): that
+      // CTA's rows belong to the next group and must not be stored
+      const bool beyond = mt * RB + BM * crank >= Cfg::ROWS_PER_PAIR * align_up(S.cnt[e], 128);
       const float w_pair = MODE == 2 ? tbuf[128 + (r >> 1)] : 0.f;
       const int tok_pair = MODE == 2 ? reinterpret_cast<const int*>(tbuf)[64 + (r >> 1)] : 0;
       __syncwarp();
@@ -585,20 +703,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           // that arrives last sums all of them and runs the epilogue.
           const int sp = S.splits;
           float4* part = reinterpret_cast<float4*>(args.split_partial);
-          const size_t base = (size_t)slot * (EPI_WARPS * 32 * 32) + (size_t)ew * 32 * 32 + lane;
+          const int pslot = PAIR ? 2 * slot + crank : slot;   // each CTA of a pair keeps its own half
+          const size_t base = (size_t)pslot * (EPI_WARPS * 32 * 32) + (size_t)ew * 32 * 32 + lane;
 #pragma unroll
           for (int j4 = 0; j4 < 32; ++j4)
             __stcg(part + base + 32 * j4, make_float4(acc[4 * j4], acc[4 * j4 + 1], acc[4 * j4 + 2], acc[4 * j4 + 3]));
           __threadfence();
           named_barrier_sync(kEpiBarrier, EPI_WARPS * 32);
-          if (ew == 0 && lane == 0) S.split_last[tb] = atomicAdd(args.split_cnt + tail_i, 1) == sp - 1;
+          if (ew == 0 && lane == 0)
+            S.split_last[tb] = atomicAdd(args.split_cnt + (PAIR ? 2 * tail_i + crank : tail_i), 1) == sp - 1;
           named_barrier_sync(kEpiBarrier, EPI_WARPS * 32);
           if (!S.split_last[tb]) continue;
           __threadfence();
           const int first = slot - (slot % sp);
           for (int o = first; o < first + sp; ++o) {
             if (o == slot) continue;
-            const size_t ob = (size_t)o * (EPI_WARPS * 32 * 32) + (size_t)ew * 32 * 32 + lane;
+            const size_t ob = (size_t)(PAIR ? 2 * o + crank : o) * (EPI_WARPS * 32 * 32) + (size_t)ew * 32 * 32 + lane;
 #pragma unroll
             for (int j4 = 0; j4 < 32; ++j4) {
               const float4 v = __ldcg(part + ob + 32 * j4);
@@ -666,8 +786,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0 && MOE_DCHECK(row_off_e + mt * BM + 32 * q + 32 <= args.R1, args.err)) {
-          const int y = row_off_e + mt * BM + 32 * q;         // pair row of the warp's first row
+        if (lane == 0 && !beyond && MOE_DCHECK(row_off_e + mt * RB + BM * crank + 32 * q + 32 <= args.R1, args.err)) {
+          const int y = row_off_e + mt * RB + BM * crank + 32 * q;   // pair row of the warp's first row
           tma_store_2d(&tmOut, smem_u32(box_hi), nt * 128 + 64 * g, y);
           tma_store_2d(&tmOut, smem_u32(box_lo), kInter + nt * 128 + 64 * g, y);
           bulk_commit();
@@ -721,27 +841,80 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (MODE == 1 && warp >= 2 && warp < 2 + EPI_WARPS && lane == 0) bulk_wait_all();   // output tiles written
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves while the other may still signal its barriers
+  if (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
-static int g_smem_set[2][64];
+static int g_smem_set[2][2][64];
+static int g_clusters[2][64];
 
-template <int MODE>
+// CTA-pair tile kernels: off unless $MOE_CTA_PAIR=1 at first use.
+int g_cta_pair = -1;
+bool cta_pair_enabled() {
+  if (g_cta_pair < 0) {
+    const char* e = getenv("MOE_CTA_PAIR");
+    g_cta_pair = (e && atoi(e) == 1) ? 1 : 0;
+  }
+  return g_cta_pair == 1;
+}
+
+template <int MODE, bool PAIR>
 cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
                           const GemmArgs& args, int num_sms, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !g_smem_set[MODE - 1][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gemm_smem_bytes<MODE>());
+  auto kern = grouped_gemm_kernel<MODE, PAIR>;
+  const size_t smem = gemm_smem_bytes<MODE, PAIR>();
+  if (dev >= 64 || !g_smem_set[MODE - 1][PAIR][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    if (dev < 64) g_smem_set[MODE - 1][dev] = 1;
+    if (dev < 64) g_smem_set[MODE - 1][PAIR][dev] = 1;
   }
-  return launch_kernel(grouped_gemm_kernel<MODE>, dim3(num_sms), dim3(GEMM_THREADS), gemm_smem_bytes<MODE>(), st, true, tmA,
-                       tmB, tmOut, args);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int nattr = 1;
+  int grid = num_sms;
+  if (PAIR) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    nattr = 2;
+    // as many pairs as can be resident at once (a persistent grid must not wait for a second wave)
+    int clusters = dev < 64 ? g_clusters[MODE - 1][dev] : 0;
+    if (clusters == 0) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(num_sms & ~1);
+      q.blockDim = dim3(GEMM_THREADS);
+      q.dynamicSmemBytes = smem;
+      q.attrs = &attr[1];
+      q.numAttrs = 1;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kern, &q);
+      if (e != cudaSuccess || clusters < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
+      clusters = min(clusters, num_sms / 2);
+#ifdef XPRINT_CLUSTERS
+      fprintf(stderr, "PAIRLAUNCH mode=%d max_active_clusters=%d smem=%zu\n", MODE, clusters, smem);
+#endif
+      if (dev < 64) g_clusters[MODE - 1][dev] = clusters;
+    }
+    grid = 2 * clusters;
+  }
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmOut, args);
 }
 
 cudaError_t set_debug_waits_tile(unsigned long long limit_ns, int gate_extra) {
@@ -763,11 +936,14 @@ cudaError_t read_trace(unsigned long long* host, int n) {
 
 cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
                          const GemmArgs& args, int num_sms, cudaStream_t st) {
-  return launch_gemm_t<1>(tmA, tmB, tmOut, args, num_sms, st);
+  return cta_pair_enabled() ? launch_gemm_t<1, true>(tmA, tmB, tmOut, args, num_sms, st)
+                            : launch_gemm_t<1, false>(tmA, tmB, tmOut, args, num_sms, st);
 }
 cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
                          cudaStream_t st) {
-  return launch_gemm_t<2>(tmA, tmB, tmA, args, num_sms, st);   // GEMM2 stores no tiles
+  // GEMM2 stores no tiles
+  return cta_pair_enabled() ? launch_gemm_t<2, true>(tmA, tmB, tmA, args, num_sms, st)
+                            : launch_gemm_t<2, false>(tmA, tmB, tmA, args, num_sms, st);
 }
 
 }  // namespace moe

@@ -251,7 +251,8 @@ int make_plan(const MoeFp8Args* a, Plan& p, const int* given_idx = nullptr, cons
   p.pair_out = p.det ? reinterpret_cast<float*>(w + L.pair_out) : nullptr;
   p.path = gemm_path(T);
   const bool s1 = p.path != 0, s2 = p.path >= 2;
-  const uint32_t w2_box = s2 ? 128 : 256;
+  // the CTA-pair tile kernels load 128 W2 rows per CTA
+  const uint32_t w2_box = (s2 || moe::cta_pair_enabled()) ? 128 : 256;
   // streaming kernels: 128-byte boxes, 128-byte swizzle; tile kernels: boxes as wide as their stages
   const uint32_t c1 = s1 ? 128 : moe::kTileStageK1, c2 = s2 ? 128 : moe::kTileStageK2;
   if (!encode_fp8_2d(&p.tmA1, p.a1, moe::kHidden, L.R1, s1 ? 16 : 128, c1) ||

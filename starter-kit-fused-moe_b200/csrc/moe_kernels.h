@@ -90,6 +90,8 @@ cudaError_t read_trace(unsigned long long* host, int n);
 // each pair), 32 x 64-byte boxes, 64-byte swizzle; GEMM1 stores its output tiles through it.
 cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
                          const GemmArgs& args, int num_sms, cudaStream_t st);
+// Whether the tile GEMMs run as CTA pairs (256-row tiles over two SMs).
+bool cta_pair_enabled();
 cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
                          cudaStream_t st);
 
