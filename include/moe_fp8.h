@@ -103,6 +103,18 @@ int32_t moe_fp8_set_gemm_path(int32_t path);
  * gather-reduce (cutlass_large_path.py:140-179). */
 int32_t moe_fp8_set_deterministic(int32_t on);
 
+/* Run the 128-row tile GEMMs as CTA pairs (1) or single CTAs (0, the default;
+ * also $MOE_CTA_PAIR=1 at load); returns the previous setting. A pair is a
+ * two-CTA cluster computing a 256-row tile with tcgen05.mma.cta_group::2: each
+ * CTA loads its own 128 rows of activations and half of the weight tile (32 KB
+ * per K-block instead of 48 KB), the leader issues the MMA, and each CTA
+ * promotes and stores its own 128 rows. Same results within the parity bar;
+ * not faster on this workload (see the design notes), hence off. Takes effect
+ * for later calls; the workspace is unchanged. The reference's CuTe K13 kernel
+ * shares operand tiles across a (1, 4) cluster instead
+ * (solution/triton/cutlass_gemm1_helper.py:326-333). */
+int32_t moe_fp8_set_cta_pair(int32_t on);
+
 /* Workspace bytes for up to `max_tokens` tokens and `num_local_experts` experts.
  * The reference keeps an equivalent op-owned cache (solution/cuda/kernel.cu:25-56,
  * solution/triton/current_kernel.py:186-208); here the caller owns it. */

@@ -68,7 +68,7 @@ EXPORTED_SYMBOLS = (
     "moe_fp8_read_device_error", "moe_fp8_last_error", "moe_fp8_kernels_per_call", "moe_fp8_run_stage",
     "moe_fp8_set_gemm_path", "moe_fp8_gemm_path", "moe_fp8_route_static",
     "moe_fp8_ep_plan", "moe_fp8_ep_pack", "moe_fp8_ep_scales", "moe_fp8_ep_combine",
-    "moe_fp8_quantize_activations", "moe_fp8_set_deterministic", "moe_fp8_debug_set_waits",
+    "moe_fp8_quantize_activations", "moe_fp8_set_deterministic", "moe_fp8_debug_set_waits", "moe_fp8_set_cta_pair",
     "moe_fp8_block_scale_run_routed", "moe_fp8_ep_peer_buffer_bytes", "moe_fp8_ep_peer_buffer_alloc",
     "moe_fp8_ep_peer_buffer_free", "moe_fp8_ep_peer_ipc_handle", "moe_fp8_ep_peer_ipc_open",
     "moe_fp8_ep_peer_ipc_close", "moe_fp8_ep_peer_recv_view", "moe_fp8_ep_peer_dispatch", "moe_fp8_ep_peer_wait",
@@ -108,6 +108,8 @@ def load_library(path: str | pathlib.Path | None = None) -> ctypes.CDLL:
         lib.moe_fp8_last_error.restype = ctypes.c_char_p
         lib.moe_fp8_set_gemm_path.argtypes = [i32]
         lib.moe_fp8_set_gemm_path.restype = i32
+        lib.moe_fp8_set_cta_pair.argtypes = [i32]
+        lib.moe_fp8_set_cta_pair.restype = i32
         lib.moe_fp8_set_deterministic.argtypes = [i32]
         lib.moe_fp8_set_deterministic.restype = i32
         lib.moe_fp8_gemm_path.argtypes = [i32]
@@ -304,6 +306,11 @@ def set_deterministic(on: bool) -> bool:
 def set_gemm_path(path: int) -> int:
     """Force a GEMM kernel family (0..3, see GEMM_PATHS) or -1 for automatic; returns the previous setting."""
     return int(load_library().moe_fp8_set_gemm_path(int(path)))
+
+
+def set_cta_pair(on: bool) -> bool:
+    """Run the tile GEMMs as two-CTA clusters (see moe_fp8_set_cta_pair); returns the previous setting."""
+    return bool(load_library().moe_fp8_set_cta_pair(1 if on else 0))
 
 
 def gemm_path(num_tokens: int) -> int:

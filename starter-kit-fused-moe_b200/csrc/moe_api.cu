@@ -417,6 +417,8 @@ int32_t moe_fp8_set_gemm_path(int32_t path) {
 
 int32_t moe_fp8_gemm_path(int32_t num_tokens) { return gemm_path(num_tokens); }
 
+int32_t moe_fp8_set_cta_pair(int32_t on) { return moe::set_cta_pair(on); }
+
 int32_t moe_fp8_set_deterministic(int32_t on) {
   const int32_t old = deterministic() ? 1 : 0;
   g_deterministic.store(on ? 1 : 0, std::memory_order_relaxed);

@@ -92,6 +92,7 @@ cudaError_t launch_gemm1(const CUtensorMap& tmA, const CUtensorMap& tmB, const C
                          const GemmArgs& args, int num_sms, cudaStream_t st);
 // Whether the tile GEMMs run as CTA pairs (256-row tiles over two SMs).
 bool cta_pair_enabled();
+int set_cta_pair(int on);   // returns the previous setting
 cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
                          cudaStream_t st);
 

@@ -285,3 +285,50 @@ def test_streaming_path_leaves_routing_intact(pkg, gpu_inputs):
     idx, w, _ = pkg.route(x.routing_logits, x.routing_bias, 0, 32, 2.5)
     assert torch.equal(idx_after, idx)
     assert torch.equal(w_after, w)
+
+
+@pytest.fixture
+def cta_pair(pkg):
+    old_pair = pkg.set_cta_pair(True)
+    old_path = pkg.set_gemm_path(0)
+    yield
+    pkg.set_gemm_path(old_path)
+    pkg.set_cta_pair(old_pair)
+
+
+@pytest.mark.parametrize("T,seed,skewed", [(200, 51, False), (600, 7, True), (1000, 3, False)])
+def test_cta_pair_tile_kernels_match_oracle(T, seed, skewed, cta_pair, pkg, oracle):
+    """The two-CTA (tcgen05 cta_group::2) tile kernels: 256-row tiles whose second
+    half may start past an expert's 128-row group (not stored), K-split tails."""
+    x = pkg.inputs.make_inputs(T, seed=seed, device="cuda", skewed=skewed)
+    outs = [pkg.run(*x.args()) for _ in range(2)]
+    torch.cuda.synchronize()
+    assert pkg.read_device_error() == 0
+    ref = oracle.moe_forward(*x.args())
+    for o in outs:
+        err = assert_close(o.float().cpu().numpy(), ref, what=f"cta pair T={T}")
+    print(f"cta pair T={T}: max_abs_err={err:.3e}")
+
+
+def test_cta_pair_benchmark_config_sampled_rows(cta_pair, pkg, oracle):
+    x = pkg.inputs.make_inputs(4096, seed=0, device="cuda")
+    out = pkg.run(*x.args())
+    torch.cuda.synchronize()
+    assert pkg.read_device_error() == 0
+    rows, xs = sampled_rows(oracle, x, n=96)
+    err = assert_close(out[torch.from_numpy(rows).cuda()].float().cpu().numpy(), oracle.moe_forward(*xs.args()),
+                       what="cta pair T=4096 sampled rows")
+    print(f"cta pair T=4096: max_abs_err={err:.3e}")
+
+
+def test_cta_pair_deterministic_combine(cta_pair, pkg, oracle):
+    old = pkg.set_deterministic(True)
+    try:
+        x = pkg.inputs.make_inputs(600, seed=5, device="cuda", skewed=True)
+        outs = [pkg.run(*x.args()).clone() for _ in range(2)]
+        torch.cuda.synchronize()
+    finally:
+        pkg.set_deterministic(old)
+    assert pkg.read_device_error() == 0
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    assert_close(outs[0].float().cpu().numpy(), oracle.moe_forward(*x.args()), what="cta pair deterministic")
