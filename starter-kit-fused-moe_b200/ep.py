@@ -375,6 +375,8 @@ class PeerExpertParallel:
         self._opened = []
         self.base = base if base is not None else self.K.alloc(self.capacity, self.world)
         self._own_base = base is None
+        self._group = group
+        self._mapped_over_group = peer_bases is None
         if peer_bases is None:
             handles = [None] * self.world
             dist.all_gather_object(handles, self.K.handle(self.base), group=group)
@@ -391,8 +393,23 @@ class PeerExpertParallel:
         self.peer_bases = bases
         self.peers = self.K.peer_table(bases)
 
-    def dispatch(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+    @staticmethod
+    def _check_tokens(routing_logits, routing_bias, hidden_states, hidden_states_scale):
+        """The kernels read these through raw pointers: shapes, dtypes and layouts must be exact."""
         T = int(routing_logits.shape[0])
+        checks = ((routing_logits, (T, E_GLOBAL), torch.float32, "routing_logits"),
+                  (hidden_states, (T, H), torch.float8_e4m3fn, "hidden_states"),
+                  (hidden_states_scale, (H // 128, T), torch.float32, "hidden_states_scale"))
+        for t, shape, dtype, name in checks:
+            if tuple(t.shape) != shape or t.dtype != dtype or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous {dtype} tensor of shape {shape}, "
+                                 f"got {t.dtype} {tuple(t.shape)}")
+        if routing_bias is not None and (routing_bias.numel() != E_GLOBAL or routing_bias.dtype != torch.bfloat16):
+            raise ValueError("routing_bias must be bf16 with 256 entries (or None)")
+        return T
+
+    def dispatch(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+        T = self._check_tokens(routing_logits, routing_bias, hidden_states, hidden_states_scale)
         if T > self.capacity:
             raise ValueError(f"{T} tokens exceed the exchange capacity {self.capacity}")
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF
@@ -421,6 +438,8 @@ class PeerExpertParallel:
         """One step for this rank's tokens; returns bf16 [T, 7168]. `marks`, a
         list, receives a CUDA event after each phase (route + dispatch, compute,
         combine) for per-phase timing."""
+        if int(gemm1_weights.shape[0]) != self.epr:
+            raise ValueError(f"this rank holds {self.epr} experts, got weights for {gemm1_weights.shape[0]}")
         rec = (lambda: marks.append(_event())) if marks is not None else (lambda: None)
         rec()
         self.dispatch(routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor)
@@ -440,6 +459,13 @@ class PeerExpertParallel:
         return self.K.read_error(self)
 
     def close(self):
+        """Unmap the peers' buffers and free this rank's. With buffers mapped
+        over a process group every rank must call it (a barrier keeps a buffer
+        alive until no peer can still write into it)."""
+        if self._mapped_over_group and self.base is not None:
+            if torch.cuda.is_available() and isinstance(self.base, int):
+                torch.cuda.synchronize()
+            dist.barrier(group=self._group)
         for b in self._opened:
             self.K.close(b)
         self._opened = []
