@@ -36,7 +36,6 @@
 //          reductions (cp.reduce.async.bulk .add.f32), so the top-k combine
 //          happens here, with no separate reduce pass, and overlaps the next
 //          tile's main loop.
-#include <cstdio>
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 #include "moe_workspace.h"
@@ -890,9 +889,6 @@ cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
       cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kern, &q);
       if (e != cudaSuccess || clusters < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
       clusters = min(clusters, num_sms / 2);
-#ifdef XPRINT_CLUSTERS
-      fprintf(stderr, "PAIRLAUNCH mode=%d max_active_clusters=%d smem=%zu\n", MODE, clusters, smem);
-#endif
       if (dev < 64) g_clusters[MODE - 1][dev] = clusters;
     }
     grid = 2 * clusters;
