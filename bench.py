@@ -40,7 +40,7 @@ L2_FLUSH_BYTES = 256 << 20
 # `ncu --set full --clock-control none -k regex:stream_gemm_kernel -s 2 -c 1`
 # capture of `python bench.py --steps 3 --warmup 3 --no-sweep --no-cpu-baseline`.
 # Other token counts have no capture, so their `traffic` is reported as null.
-STREAM_TRAFFIC_BYTES_T64 = 763_864_064 + 8_500_736
+STREAM_TRAFFIC_BYTES_T64 = 764_299_520 + 7_048_192
 
 
 def load_peaks():
